@@ -1,0 +1,311 @@
+"""Benchmark of the packed block-masked prefill attention (cfg2 shape).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+One step = one packed attention call over 32 requests x (2048-token cached
+prefix + 16 suffixes x 64 tokens), Hq 16 / Hkv 8, head_dim 128, bf16, on
+seeded synthetic Q/K/V (N(0,1), RMS-normalised per head, RoPE at positions
+restarting at 2048 per suffix).  The metric is effective TFLOP/s:
+4 * D * Hq * (visible query-key pairs) per call = 5.585e11 FLOP; masked pairs
+do not count.  With --gpus N (torchrun, one rank per GPU) every rank runs its
+own batch (weak scaling, no collective on the data path); the time is the max
+over ranks.
+
+`value` is kernel throughput with inputs resident in HBM; `e2e` is the same
+metric through the C ABI call with host buffers: pinned host -> device copies
+of Q, K, V and the segment table, the call, and the device -> host copy of O
+inside the timed region.  `--impl reference` times the reference algorithm
+(the CPU oracle: repeat_kv + matmul + additive mask + softmax + matmul,
+qwen3.rs:206-220) on the host cores on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rust-cev_b200"))
+
+METRIC = "packed-prefill attn TFLOP/s (% BF16 peak); decisions/sec at 1/2/4/8 B200"
+CFG = dict(n_req=32, prefix=2048, n_suf=16, suf_len=64, hq=16, hkv=8, head_dim=128)
+WORKLOAD = "cfg2 packed-prefill attention: 32 requests x (2048-token prefix + 16 x 64-token suffixes), Hq16/Hkv8, D128"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "attn_tc_cfg2.md")
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_reference(args, rank, world):
+    """The reference algorithm on the host cores (CPU oracle, f32)."""
+    if rank != 0:
+        return
+    import torch
+    sys.path.insert(0, ROOT)
+    from oracle import ops as ref
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    c = CFG
+    g = torch.Generator().manual_seed(0)
+    D, hq, hkv, P, L = c["head_dim"], c["hq"], c["hkv"], c["prefix"], c["suf_len"]
+    n_suf = 2  # bounded sample: one request's prefix with 2 of its suffixes per step
+
+    def rn(*s):
+        x = torch.randn(*s, generator=g)
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+    k = rn(1, hkv, P + n_suf * L, D)
+    v = torch.randn(1, hkv, P + n_suf * L, D, generator=g)
+    q = rn(1, hq, n_suf * L, D)
+    # one request packed the reference way: K/V concatenated, additive mask
+    # over [prefix | all suffixes], each suffix sees the prefix and itself causally
+    mask = ref.segment_mask(sum([[j] * L for j in range(n_suf)], []), P)
+    flops = 4.0 * D * hq * n_suf * (L * P + L * (L + 1) // 2)
+
+    def step():
+        ref.attend(q, k, v, mask)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    val = flops / dt / 1e12
+    sample = f"{n_suf} of 512 suffixes (1 request prefix) per step, f32, torch CPU, {cores} threads"
+    line = {"metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "sample": sample},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample():
+    """Reference algorithm on a bounded sample (rank 0, N=1 only)."""
+    import torch
+    sys.path.insert(0, ROOT)
+    from oracle import ops as ref
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    c = CFG
+    g = torch.Generator().manual_seed(0)
+    D, hq, hkv, P, L, n_suf = c["head_dim"], c["hq"], c["hkv"], c["prefix"], c["suf_len"], 4
+    x = torch.randn(1, hkv, P + n_suf * L, D, generator=g)
+    q = torch.randn(1, hq, n_suf * L, D, generator=g)
+    mask = ref.segment_mask(sum([[j] * L for j in range(n_suf)], []), P)
+    flops = 4.0 * D * hq * n_suf * (L * P + L * (L + 1) // 2)
+    ref.attend(q, x, x, mask)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0:
+        ref.attend(q, x, x, mask)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"1 request prefix + {n_suf} suffixes, f32 torch CPU, {reps} reps over ~10 s"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="cevk")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from cev_b200 import ops, workloads
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    wb = workloads.AttentionBatch(seed=1000 + rank, device=dev, **CFG)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        wb.run()
+    torch.cuda.synchronize()
+    ops.device_status()
+
+    # ---------------- device-resident timing ----------------
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t_all0 = torch.cuda.Event(enable_timing=True)
+        t_all1 = torch.cuda.Event(enable_timing=True)
+        t_all0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            wb.run()
+            ends[i].record(stream)
+        t_all1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = t_all0.elapsed_time(t_all1)
+    kern_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    t = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = t.item()
+    ms_step = total_ms / args.steps
+    value = world * wb.flops * args.steps / (total_ms / 1e3) / 1e12
+    ops.device_status()
+
+    # ---------------- end to end through the C ABI, host buffers ----------------
+    import ctypes as C
+    from cev_b200._lib import BF16, check, lib
+    hq_, hk, hv = (wb.q.cpu().pin_memory(), wb.k.cpu().pin_memory(), wb.v.cpu().pin_memory())
+    hseg = wb.plan.host.pin_memory()
+    ho = torch.empty_like(hq_).pin_memory()
+    dq, dk, dv, do = (torch.empty_like(wb.q), torch.empty_like(wb.k), torch.empty_like(wb.v), torch.empty_like(wb.q))
+    dseg = torch.empty_like(wb.plan.dev)
+    h2d = sum(x.numel() * x.element_size() for x in (hq_, hk, hv, hseg))
+    d2h = ho.numel() * ho.element_size()
+
+    def e2e_step():
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dseg.copy_(hseg, non_blocking=True)
+        check(lib().cevk_attn_packed_prefill(
+            C.c_void_p(dq.data_ptr()), C.c_void_p(dk.data_ptr()), C.c_void_p(dv.data_ptr()), C.c_void_p(do.data_ptr()),
+            wb.n_tokens, wb.n_kv, wb.hq, wb.hkv, wb.D, dq.stride(0), dk.stride(0), do.stride(0),
+            C.c_void_p(dseg.data_ptr()), wb.plan.n_segs, wb.plan.n_tiles, 1.0 / wb.D ** 0.5, BF16,
+            C.c_void_p(stream.cuda_stream)))
+        ho.copy_(do, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_steps = max(3, min(args.steps, 20))
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_val = world * wb.flops * e_steps / (e_ms.item() / 1e3) / 1e12
+    if not torch.equal(ho.to(dev), wb.out):
+        raise RuntimeError("end-to-end output differs from the device-resident output")
+
+    peak_tf, peak_hbm, src = peaks()
+    avg_kern = statistics.mean(kern_ms[1:] if len(kern_ms) > 1 else kern_ms)
+    achieved = wb.flops / (avg_kern / 1e3) / 1e12
+    tr = profiled_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "flop_per_step_per_gpu": wb.flops,
+                   "l2": "inputs larger than L2 (Q+K+V+O = %.0f MB per GPU)" % (
+                       (2 * wb.q.numel() + wb.k.numel() + wb.v.numel()) * 2 / 1e6),
+                   "parallelism": f"dp{world} (independent request batches, no collective)"},
+        "pct_of_bf16_peak": 100.0 * (value / world) / peak_tf,
+        "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tf, "peak_source": src + " bf16 burst",
+                     "traffic": tr, "algorithmic_bytes": wb.algorithmic_bytes()},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,80 @@
+"""Seeded synthetic workloads with the benchmark shapes.
+
+``attention_batch`` builds the packed-prefill attention microbenchmark
+(cfg2): ``n_req`` requests, each a cached prefix of ``prefix`` K/V rows plus
+``n_suf`` question suffixes of ``suf_len`` tokens.  Q/K/V are drawn N(0, 1);
+Q and K are RMS-normalised per head and rotated with RoPE at their positions
+(prefix rows at 0..P-1, every suffix restarting at P) by the library's own
+norm+RoPE kernel, which also writes K/V into the arena.  Arena layout per
+request: its prefix rows, then its suffixes' rows.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+def visible_pairs(prefix: int, suf_lens) -> int:
+    """(query, key) pairs a suffix batch attends to: the whole prefix plus a
+    causal triangle over itself."""
+    return sum(n * prefix + n * (n + 1) // 2 for n in suf_lens)
+
+
+def attention_flops(hq: int, head_dim: int, pairs: int) -> float:
+    """Effective FLOPs: QK^T and PV, 2 flops per MAC, visible pairs only."""
+    return 4.0 * head_dim * hq * pairs
+
+
+class AttentionBatch:
+    def __init__(self, n_req=32, prefix=2048, n_suf=16, suf_len=64, hq=16, hkv=8, head_dim=128, seed=0,
+                 dtype=torch.bfloat16, device="cuda", theta=1e6):
+        self.n_req, self.prefix, self.n_suf, self.suf_len = n_req, prefix, n_suf, suf_len
+        self.hq, self.hkv, self.D = hq, hkv, head_dim
+        D = head_dim
+        per_req_q = n_suf * suf_len
+        per_req_kv = prefix + per_req_q
+        self.n_tokens = n_req * per_req_q
+        self.n_kv = n_req * per_req_kv
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.q = torch.empty(self.n_tokens, hq, D, dtype=dtype, device=device)
+        self.k = torch.empty(self.n_kv, hkv, D, dtype=dtype, device=device)
+        self.v = torch.empty(self.n_kv, hkv, D, dtype=dtype, device=device)
+        ones_d = torch.ones(D, dtype=dtype, device=device)
+        # Prefix rows of every request (positions 0..P-1): K/V only.
+        if prefix > 0:
+            raw = torch.randn(n_req * prefix, (hq + 2 * hkv) * D, generator=gen, device=device).to(dtype)
+            pos = torch.arange(prefix, device=device, dtype=torch.int32).repeat(n_req)
+            rows = (torch.arange(n_req, device=device, dtype=torch.int32)[:, None] * per_req_kv
+                    + torch.arange(prefix, device=device, dtype=torch.int32)[None, :]).reshape(-1)
+            scratch_q = torch.empty(n_req * prefix, hq, D, dtype=dtype, device=device)
+            ops.qk_norm_rope(raw, (0, D), hq * D, (hq + hkv) * D, hq, hkv, D, ones_d, ones_d, 1e-6, False, pos, theta,
+                             D, scratch_q, self.k, self.v, rows)
+            del scratch_q, raw
+        # Suffix rows: queries and their own K/V; positions restart at P.
+        raw = torch.randn(self.n_tokens, (hq + 2 * hkv) * D, generator=gen, device=device).to(dtype)
+        pos = (prefix + torch.arange(suf_len, device=device, dtype=torch.int32)).repeat(n_req * n_suf)
+        r = torch.arange(n_req, device=device, dtype=torch.int32)[:, None] * per_req_kv + prefix
+        rows = (r + torch.arange(per_req_q, device=device, dtype=torch.int32)[None, :]).reshape(-1)
+        ops.qk_norm_rope(raw, (0, D), hq * D, (hq + hkv) * D, hq, hkv, D, ones_d, ones_d, 1e-6, False, pos, theta, D,
+                         self.q, self.k, self.v, rows)
+        del raw
+        self.segments = []
+        for rq in range(n_req):
+            for j in range(n_suf):
+                self.segments.append((rq * per_req_q + j * suf_len, suf_len, rq * per_req_kv, prefix,
+                                      rq * per_req_kv + prefix + j * suf_len))
+        self.plan = ops.AttnPlan(self.segments, self.n_tokens, self.n_kv, hq, hkv, D, dtype, device)
+        self.pairs = visible_pairs(prefix, [suf_len] * (n_req * n_suf))
+        self.flops = attention_flops(hq, D, self.pairs)
+        self.out = torch.empty_like(self.q)
+
+    def run(self):
+        return ops.attend_packed(self.q, self.k, self.v, self.plan, out=self.out)
+
+    def algorithmic_bytes(self) -> int:
+        """Bytes a perfect kernel moves per call: Q and O once, each
+        request's K/V rows once."""
+        e = self.q.element_size()
+        return e * (2 * self.q.numel() + self.k.numel() + self.v.numel())

@@ -1,0 +1,110 @@
+// The C ABI: status codes, thread-local error messages, host-side
+// validation of shapes and descriptors, and dispatch to the kernels.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+namespace cevk {
+
+__device__ int g_device_error = 0;
+
+static thread_local char g_msg[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
+int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
+                   int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
+                   cudaStream_t stream);
+int attn_simt_launch(const void* q, const void* k, const void* v, void* o, int hq, int hkv, int D, int q_rs, int kv_rs,
+                     int o_rs, const cevk_segment* segs, int n_segs, float scale, cudaStream_t stream);
+
+}  // namespace cevk
+
+using namespace cevk;
+
+extern "C" {
+
+const char* cevk_last_error(void) { return g_msg; }
+
+int cevk_version(void) { return 100; }
+
+int cevk_device_status(void) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "device: %s", cudaGetErrorString(e));
+  int flag = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&flag, g_device_error, sizeof(int)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess)
+    return set_error(CEVK_E_CUDA, "cannot read the device error flag");
+  if (flag) return set_error(CEVK_E_TIMEOUT, "a bounded device wait gave up (code %d)", flag);
+  return CEVK_OK;
+}
+
+int cevk_attn_schedule(cevk_segment* segs, int32_t n_segs, int32_t n_tokens, int32_t n_kv_rows, int32_t hq,
+                       int32_t hkv, int32_t head_dim, int32_t dtype, int32_t* n_tiles) {
+  if (!segs || n_segs < 0 || !n_tiles) return set_error(CEVK_E_SHAPE, "schedule: null argument");
+  if (hkv <= 0 || hq % hkv != 0) return set_error(CEVK_E_SHAPE, "hq (%d) must be a multiple of hkv (%d)", hq, hkv);
+  const int group = hq / hkv;
+  int rows_t = 1;
+  if (dtype == CEVK_BF16) {
+    if (128 % group != 0) return set_error(CEVK_E_SHAPE, "bf16 attention needs hq/hkv dividing 128 (got %d)", group);
+    rows_t = 128 / group;
+  }
+  int64_t tiles = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    const cevk_segment& g = segs[i];
+    if (g.q_len < 0 || g.prefix_len < 0 || g.q_start < 0 || g.prefix_off < 0 || g.self_off < 0)
+      return set_error(CEVK_E_RANGE, "segment %d: negative offset or length", i);
+    if ((int64_t)g.q_start + g.q_len > n_tokens)
+      return set_error(CEVK_E_RANGE, "segment %d: query rows %d..%d past %d tokens", i, g.q_start, g.q_start + g.q_len, n_tokens);
+    if ((int64_t)g.prefix_off + g.prefix_len > n_kv_rows || (int64_t)g.self_off + g.q_len > n_kv_rows)
+      return set_error(CEVK_E_RANGE, "segment %d: K/V rows past %d", i, n_kv_rows);
+    segs[i].tile_start = (int32_t)tiles;
+    tiles += (segs[i].q_len + rows_t - 1) / rows_t;
+  }
+  if (tiles > (1ll << 30)) return set_error(CEVK_E_RANGE, "too many tiles");
+  *n_tiles = (int32_t)tiles;
+  (void)head_dim;
+  return CEVK_OK;
+}
+
+int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
+                             int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
+                             int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
+                             int32_t n_segs, int32_t n_tiles, float scale, int32_t dtype, void* stream) {
+  if (!q || !k || !v || !o || (!segs_dev && n_segs > 0)) return set_error(CEVK_E_SHAPE, "attention: null pointer");
+  if (hkv <= 0 || hq % hkv != 0) return set_error(CEVK_E_SHAPE, "hq (%d) must be a multiple of hkv (%d)", hq, hkv);
+  if (q_row_stride < hq * head_dim || o_row_stride < hq * head_dim || kv_row_stride < hkv * head_dim)
+    return set_error(CEVK_E_SHAPE, "attention: row stride smaller than heads * head_dim");
+  if (n_segs == 0 || n_tiles == 0) return CEVK_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CEVK_BF16) {
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15)
+      return set_error(CEVK_E_SHAPE, "attention: q/k/v must be 16-byte aligned");
+    if ((q_row_stride % 8) || (kv_row_stride % 8))
+      return set_error(CEVK_E_SHAPE, "attention: bf16 row strides must be multiples of 8 elements");
+    if (128 % (hq / hkv) != 0) return set_error(CEVK_E_SHAPE, "attention: hq/hkv must divide 128");
+    return attn_tc_launch(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
+                          segs_dev, n_segs, n_tiles, scale, st);
+  }
+  if (dtype == CEVK_F32)
+    return attn_simt_launch(q, k, v, o, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride, segs_dev, n_segs,
+                            scale, st);
+  return set_error(CEVK_E_UNSUPPORTED, "attention: dtype %d", dtype);
+}
+
+}  // extern "C"

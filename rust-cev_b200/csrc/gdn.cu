@@ -1,0 +1,341 @@
+// Gated DeltaNet chunked prefill (qwen35.rs:301-368 and the prologue /
+// epilogue of GatedDeltaNet::forward, qwen35.rs:419-451), all arithmetic in
+// f32 like the reference.
+//
+// Kernel 1, gdn_chunk_kernel: one CTA per (row b, value head h, slice of 32
+// value columns).  The columns of the recurrent state S (dk x dv), of v_new
+// and of the output are independent, so a head's sequential scan over its
+// 64-token chunks is split over dv/32 CTAs (128 CTAs for one 32-head row).
+// Per chunk, in shared memory:
+//   q, k <- l2norm (q * dk^-1/2), beta = sigmoid(b), g = -exp(A_log) *
+//   softplus(a + dt_bias), cum = cumsum(g);
+//   A = strict_lower((k*beta) k^T o exp(cum_i - cum_j)), T = (I + A)^-1
+//   (column-wise forward substitution -- the same inverse the reference
+//   builds by recursive block inversion, qwen35.rs:266-296);
+//   U = T (v*beta), W = T (k*beta*exp(cum)), intra = lower(q k^T o decay);
+//   v_new = U - W S;  out = (q*exp(cum)) S + intra v_new;
+//   S = S*exp(cum_last) + (k*exp(cum_last - cum))^T v_new.
+// The raw f32 output goes to the caller's workspace.
+// Kernel 2, gdn_gated_norm_kernel: y = rmsnorm(out) * w * silu(z) per head,
+// cast to the model dtype (qwen35.rs:446-451).
+#include "common.cuh"
+
+namespace cevk {
+
+constexpr int GC = 64;    // chunk length (qwen35.rs:302)
+constexpr int GDVS = 32;  // value columns per CTA
+
+struct GdnParams {
+  const void* conv;  // [B, T, Cc]
+  int Cc;
+  const void* ab;  // per token: b (nv) | a (nv)
+  int ab_rs;
+  const float* a_log;
+  const float* dt_bias;
+  const float* s_in;
+  long long s_bs;
+  float* s_out;
+  float* core;  // [B, T, nv, dv] f32 workspace
+  int B, T, nk, nv, dk, dv;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnParams p) {
+  extern __shared__ float sm[];
+  const int dk = p.dk, dv = p.dv;
+  const int KP = dk + 1;  // padded row pitch (conflict-free column walks)
+  float* sQ = sm;                 // [GC][KP]
+  float* sK = sQ + GC * KP;       // [GC][KP]
+  float* sW = sK + GC * KP;       // [GC][KP]
+  float* sA = sW + GC * KP;       // [GC][GC+1]  A, then T = (I+A)^-1
+  float* sI = sA + GC * (GC + 1); // [GC][GC+1]  intra
+  float* sV = sI + GC * (GC + 1); // [GC][GDVS]  v*beta -> U -> v_new
+  float* sS = sV + GC * GDVS;     // [dk][GDVS]
+  float* sG = sS + dk * GDVS;     // cum [GC]
+  float* sB = sG + GC;            // beta [GC]
+  float* sE = sB + GC;            // beta * exp(cum) [GC]
+  const int AP = GC + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int slices = dv / GDVS;
+  const int sl = blockIdx.x % slices;
+  const int h = blockIdx.x / slices;
+  const int b = blockIdx.y;
+  const int kh = h / (p.nv / p.nk);  // k-head repeat nk -> nv (qwen35.rs:436-441)
+  const int c0 = sl * GDVS;
+  const T* conv = reinterpret_cast<const T*>(p.conv);
+  const T* ab = reinterpret_cast<const T*>(p.ab);
+  const int key_dim = p.nk * dk;
+  const float qscale = rsqrtf((float)dk);
+  const float neg_a = -expf(p.a_log[h]);
+  const float dtb = p.dt_bias[h];
+
+  // initial state slice
+  for (int i = tid; i < dk * GDVS; i += 256) {
+    const int d = i / GDVS, c = i % GDVS;
+    sS[i] = p.s_in ? p.s_in[b * p.s_bs + ((long long)h * dk + d) * dv + c0 + c] : 0.f;
+  }
+
+  const int n_chunks = (p.T + GC - 1) / GC;
+  for (int ch = 0; ch < n_chunks; ++ch) {
+    const int t0 = ch * GC;
+    __syncthreads();
+    // ---- load q, k (full dk), v slice; gates ----
+    for (int i = tid; i < GC * dk; i += 256) {
+      const int r = i / dk, d = i % dk;
+      const int t = t0 + r;
+      float qv = 0.f, kv = 0.f;
+      if (t < p.T) {
+        const T* row = conv + ((long long)b * p.T + t) * p.Cc;
+        qv = to_f(row[kh * dk + d]);
+        kv = to_f(row[key_dim + kh * dk + d]);
+      }
+      sQ[r * KP + d] = qv;
+      sK[r * KP + d] = kv;
+    }
+    if (tid < GC) {
+      const int t = t0 + tid;
+      float beta = 0.f, g = 0.f;
+      if (t < p.T) {
+        const T* row = ab + ((long long)b * p.T + t) * p.ab_rs;
+        beta = 1.f / (1.f + expf(-to_f(row[h])));
+        const float x = to_f(row[p.nv + h]) + dtb;
+        // softplus(x) = max(x, 0) + ln(1 + e^{-|x|}) (qwen35.rs:243-248)
+        g = (fmaxf(x, 0.f) + logf(1.f + expf(-fabsf(x)))) * neg_a;
+      }
+      sB[tid] = beta;
+      sG[tid] = g;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float acc = 0.f;
+      for (int r = 0; r < GC; ++r) { acc += sG[r]; sG[r] = acc; }
+    }
+    for (int i = tid; i < GC * GDVS; i += 256) {
+      const int r = i / GDVS, c = i % GDVS;
+      const int t = t0 + r;
+      float vv = 0.f;
+      if (t < p.T) vv = to_f(conv[((long long)b * p.T + t) * p.Cc + 2 * key_dim + h * dv + c0 + c]);
+      sV[i] = vv * sB[r];
+    }
+    // l2norm rows of q (then * dk^-1/2) and k: one warp per row
+    for (int r = warp; r < 2 * GC; r += 8) {
+      float* row = r < GC ? sQ + r * KP : sK + (r - GC) * KP;
+      float ss = 0.f;
+      for (int d = lane; d < dk; d += 32) ss += row[d] * row[d];
+      ss = warp_sum(ss);
+      const float inv = 1.f / sqrtf(ss + 1e-6f);
+      const float sc = r < GC ? inv * qscale : inv;
+      for (int d = lane; d < dk; d += 32) row[d] *= sc;
+    }
+    __syncthreads();
+    // ---- A (strict lower, with beta_i) and intra (lower incl. diagonal) ----
+    for (int idx = tid; idx < GC * GC; idx += 256) {
+      const int i = idx / GC, j = idx % GC;
+      float a = 0.f, q = 0.f;
+      if (j <= i) {
+        const float* ki = sK + i * KP;
+        const float* kj = sK + j * KP;
+        const float* qi = sQ + i * KP;
+        float dkk = 0.f, dqk = 0.f;
+        for (int d = 0; d < dk; ++d) {
+          dkk += ki[d] * kj[d];
+          dqk += qi[d] * kj[d];
+        }
+        const float dec = expf(sG[i] - sG[j]);
+        q = dqk * dec;
+        if (j < i) a = sB[i] * dkk * dec;
+      }
+      sA[i * AP + j] = a;
+      sI[i * AP + j] = q;
+    }
+    if (tid < GC) sE[tid] = sB[tid] * expf(sG[tid]);
+    __syncthreads();
+    // ---- T = (I + A)^-1: column c by forward substitution ----
+    if (tid < GC) {
+      const int c = tid;
+      for (int i = 0; i < GC; ++i) {
+        float x = 0.f;
+        if (i == c) x = 1.f;
+        else if (i > c) {
+          float acc = 0.f;
+          for (int j = c; j < i; ++j) acc += sA[i * AP + j] * sW[j * KP + c];  // sW column c holds T[:, c]
+          x = -acc;
+        }
+        sW[i * KP + c] = x;
+      }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < GC * GC; idx += 256) {
+      const int i = idx / GC, j = idx % GC;
+      sA[i * AP + j] = sW[i * KP + j];
+    }
+    __syncthreads();
+    // ---- U = T (v beta) (into sV via registers), W = T (k beta e^cum) ----
+    {
+      float u[GC * GDVS / 256];
+#pragma unroll
+      for (int r = 0; r < GC * GDVS / 256; ++r) {
+        const int i = warp + 8 * r, c = lane;
+        float acc = 0.f;
+        for (int j = 0; j <= i; ++j) acc += sA[i * AP + j] * sV[j * GDVS + c];
+        u[r] = acc;
+      }
+      for (int idx = tid; idx < GC * dk; idx += 256) {
+        const int i = idx / dk, d = idx % dk;
+        float acc = 0.f;
+        for (int j = 0; j <= i; ++j) acc += sA[i * AP + j] * (sK[j * KP + d] * sE[j]);
+        sW[i * KP + d] = acc;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < GC * GDVS / 256; ++r) sV[(warp + 8 * r) * GDVS + lane] = u[r];
+    }
+    // q <- q e^cum, k <- k e^(cum_last - cum)
+    const float last = sG[GC - 1];
+    for (int i = tid; i < GC * dk; i += 256) {
+      const int r = i / dk, d = i % dk;
+      sQ[r * KP + d] *= expf(sG[r]);
+      sK[r * KP + d] *= expf(last - sG[r]);
+    }
+    __syncthreads();
+    // ---- v_new = U - W S ----
+    {
+      float vn[GC * GDVS / 256];
+#pragma unroll
+      for (int r = 0; r < GC * GDVS / 256; ++r) {
+        const int i = warp + 8 * r, c = lane;
+        float acc = 0.f;
+        for (int d = 0; d < dk; ++d) acc += sW[i * KP + d] * sS[d * GDVS + c];
+        vn[r] = sV[i * GDVS + c] - acc;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < GC * GDVS / 256; ++r) sV[(warp + 8 * r) * GDVS + lane] = vn[r];
+    }
+    __syncthreads();
+    // ---- out = (q e^cum) S + intra v_new ----
+#pragma unroll
+    for (int r = 0; r < GC * GDVS / 256; ++r) {
+      const int i = warp + 8 * r, c = lane;
+      float acc = 0.f;
+      for (int d = 0; d < dk; ++d) acc += sQ[i * KP + d] * sS[d * GDVS + c];
+      float acc2 = 0.f;
+      for (int j = 0; j <= i; ++j) acc2 += sI[i * AP + j] * sV[j * GDVS + c];
+      const int t = t0 + i;
+      if (t < p.T) p.core[(((long long)b * p.T + t) * p.nv + h) * dv + c0 + c] = acc + acc2;
+    }
+    __syncthreads();
+    // ---- S = S e^last + (k e^(last-cum))^T v_new ----
+    const float el = expf(last);
+    for (int idx = tid; idx < dk * GDVS; idx += 256) {
+      const int d = idx / GDVS, c = idx % GDVS;
+      float acc = 0.f;
+      for (int j = 0; j < GC; ++j) acc += sK[j * KP + d] * sV[j * GDVS + c];
+      sS[idx] = sS[idx] * el + acc;
+    }
+  }
+  __syncthreads();
+  if (p.s_out)
+    for (int i = tid; i < dk * GDVS; i += 256) {
+      const int d = i / GDVS, c = i % GDVS;
+      p.s_out[(long long)b * p.nv * dk * dv + ((long long)h * dk + d) * dv + c0 + c] = sS[i];
+    }
+}
+
+template <typename T>
+__global__ void gdn_gated_norm_kernel(const float* __restrict__ core, const T* __restrict__ z, int z_rs,
+                                      const T* __restrict__ w, float eps, T* __restrict__ y, long long rows, int nv,
+                                      int dv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long job = (long long)blockIdx.x * (blockDim.x >> 5) + warp;  // (b*T + t) * nv + h
+  if (job >= rows * nv) return;
+  const long long bt = job / nv;
+  const int h = (int)(job % nv);
+  const float* o = core + job * dv;
+  float ss = 0.f;
+  for (int d = lane; d < dv; d += 32) ss += o[d] * o[d];
+  ss = warp_sum(ss);
+  const float r = 1.f / sqrtf(ss / dv + eps);
+  const T* zr = z + bt * z_rs + (long long)h * dv;
+  T* yr = y + bt * (long long)nv * dv + (long long)h * dv;
+  for (int d = lane; d < dv; d += 32) {
+    const float zz = to_f(zr[d]);
+    yr[d] = from_f<T>(o[d] * r * to_f(w[d]) * (zz / (1.f + expf(-zz))));
+  }
+}
+
+static size_t gdn_smem(int dk) {
+  const int KP = dk + 1;
+  return sizeof(float) * (3 * GC * KP + 2 * GC * (GC + 1) + GC * GDVS + dk * GDVS + 3 * GC);
+}
+
+}  // namespace cevk
+
+using namespace cevk;
+
+extern "C" {
+
+size_t cevk_gdn_workspace_size(int32_t B, int32_t T, int32_t nv, int32_t dk, int32_t dv) {
+  (void)dk;
+  return (size_t)B * T * nv * dv * sizeof(float);
+}
+
+int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride, const void* z,
+                           int32_t z_row_stride, const float* a_log, const float* dt_bias, const void* norm_w,
+                           float eps, const float* s_in, int64_t s_batch_stride, float* s_out, void* y, int32_t B,
+                           int32_t T, int32_t nk, int32_t nv, int32_t dk, int32_t dv, void* workspace,
+                           size_t workspace_bytes, int32_t dtype, void* stream) {
+  if (!conv_out || !ab || !z || !a_log || !dt_bias || !norm_w || !y)
+    return set_error(CEVK_E_SHAPE, "gdn: null pointer");
+  if (nk <= 0 || nv % nk || dk % 32 || dk < 64 || dk > 128 || dv % GDVS || dv > 256)
+    return set_error(CEVK_E_SHAPE, "gdn: heads %d/%d, dk %d, dv %d unsupported", nk, nv, dk, dv);
+  if (C != 2 * nk * dk + nv * dv) return set_error(CEVK_E_SHAPE, "gdn: C %d != 2*nk*dk + nv*dv", C);
+  if (B <= 0 || T <= 0) return CEVK_OK;
+  const size_t need = cevk_gdn_workspace_size(B, T, nv, dk, dv);
+  if (!workspace || workspace_bytes < need)
+    return set_error(CEVK_E_SHAPE, "gdn: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
+  GdnParams prm;
+  prm.conv = conv_out;
+  prm.Cc = C;
+  prm.ab = ab;
+  prm.ab_rs = ab_row_stride;
+  prm.a_log = a_log;
+  prm.dt_bias = dt_bias;
+  prm.s_in = s_in;
+  prm.s_bs = s_batch_stride;
+  prm.s_out = s_out;
+  prm.core = reinterpret_cast<float*>(workspace);
+  prm.B = B;
+  prm.T = T;
+  prm.nk = nk;
+  prm.nv = nv;
+  prm.dk = dk;
+  prm.dv = dv;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = gdn_smem(dk);
+  dim3 grid(nv * (dv / GDVS), B);
+  const long long rows = (long long)B * T;
+  const unsigned ng = (unsigned)((rows * nv + 7) / 8);
+  if (dtype == CEVK_BF16) {
+    cudaFuncSetAttribute(gdn_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gdn_chunk_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(prm);
+    int rc = check_launch("gdn_chunk_kernel");
+    if (rc) return rc;
+    gdn_gated_norm_kernel<__nv_bfloat16><<<ng, 256, 0, st>>>(prm.core, (const __nv_bfloat16*)z, z_row_stride,
+                                                             (const __nv_bfloat16*)norm_w, eps, (__nv_bfloat16*)y,
+                                                             rows, nv, dv);
+  } else if (dtype == CEVK_F32) {
+    cudaFuncSetAttribute(gdn_chunk_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    gdn_chunk_kernel<float><<<grid, 256, smem, st>>>(prm);
+    int rc = check_launch("gdn_chunk_kernel");
+    if (rc) return rc;
+    gdn_gated_norm_kernel<float><<<ng, 256, 0, st>>>(prm.core, (const float*)z, z_row_stride, (const float*)norm_w,
+                                                     eps, (float*)y, rows, nv, dv);
+  } else {
+    return set_error(CEVK_E_UNSUPPORTED, "gdn: dtype %d", dtype);
+  }
+  return check_launch("gdn_gated_norm_kernel");
+}
+
+}  // extern "C"

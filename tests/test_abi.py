@@ -1,0 +1,75 @@
+"""The C ABI without a GPU: the library loads, exports every entry point
+``include/cevk.h`` declares with the bound signatures, and its host-side
+validation (segment scheduling) behaves."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from cev_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "cevk.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cevk_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared()
+    assert names, "no declarations parsed"
+    for n in names:
+        assert hasattr(lib, n), f"{n} not exported"
+        assert n in _lib.SIGNATURES, f"{n} not bound in _lib.SIGNATURES"
+    assert lib.cevk_version() == 100
+
+
+def test_binding_arity_matches_header():
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    for name, (_, args) in _lib.SIGNATURES.items():
+        m = re.search(name + r"\s*\(([^)]*)\)", text)
+        assert m, name
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(args), f"{name}: header has {len(params)} params, binding {len(args)}"
+
+
+def _segs(rows):
+    arr = (_lib.Segment * len(rows))()
+    for i, r in enumerate(rows):
+        arr[i].q_start, arr[i].q_len, arr[i].prefix_off, arr[i].prefix_len, arr[i].self_off = r
+    return arr
+
+
+def test_schedule_assigns_tiles_per_gqa_group():
+    lib = _lib.lib()
+    # hq/hkv = 2 -> 64 tokens per tile; a 150-token segment needs 3 tiles.
+    arr = _segs([(0, 64, 0, 100, 100), (64, 150, 0, 100, 164), (214, 0, 0, 0, 0), (214, 1, 0, 0, 314)])
+    n = C.c_int32()
+    assert lib.cevk_attn_schedule(arr, 4, 215, 400, 16, 8, 128, _lib.BF16, C.byref(n)) == 0
+    assert [arr[i].tile_start for i in range(4)] == [0, 1, 4, 4]
+    assert n.value == 5
+
+
+@pytest.mark.parametrize("bad", [
+    (0, 65, 0, 10, 0),      # query rows past n_tokens
+    (0, 10, 390, 20, 0),    # prefix past the arena
+    (0, 10, 0, 10, 395),    # own rows past the arena
+    (-1, 10, 0, 10, 0),     # negative offset
+])
+def test_schedule_rejects_out_of_range_segments(bad):
+    lib = _lib.lib()
+    n = C.c_int32()
+    rc = lib.cevk_attn_schedule(_segs([bad]), 1, 64, 400, 16, 8, 128, _lib.BF16, C.byref(n))
+    assert rc == _lib.E_RANGE
+    assert lib.cevk_last_error().decode()
+
+
+def test_schedule_rejects_bad_gqa():
+    lib = _lib.lib()
+    n = C.c_int32()
+    assert lib.cevk_attn_schedule(_segs([(0, 1, 0, 0, 0)]), 1, 1, 1, 12, 8, 128, _lib.BF16, C.byref(n)) == _lib.E_SHAPE
+    assert lib.cevk_attn_schedule(_segs([(0, 1, 0, 0, 0)]), 1, 1, 1, 24, 8, 128, _lib.BF16, C.byref(n)) == _lib.E_SHAPE

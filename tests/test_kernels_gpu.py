@@ -1,0 +1,261 @@
+"""Kernel parity on the GPU: every op of the C ABI against the CPU oracle on
+the same seeded inputs.  Tolerances: max-abs 2e-2 for bf16 attention / GDN
+outputs and 1e-4 for f32 (the bounds the decision forward is held to)."""
+import math
+
+import pytest
+import torch
+
+from oracle import ops as ref
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+F32_TOL = 1e-4
+
+
+def cuda():
+    return torch.device("cuda")
+
+
+def oracle_segments(q, k, v, segs, scale=None):
+    """Attention per segment with the reference's generic path
+    (qwen3.rs:206-220) on CPU f32: prefix rows in full, own rows causally."""
+    q, k, v = q.float().cpu(), k.float().cpu(), v.float().cpu()
+    out = torch.zeros_like(q)
+    for (qs, ql, po, pl, so) in segs:
+        if ql == 0:
+            continue
+        kk = torch.cat([k[po:po + pl], k[so:so + ql]], 0)
+        vv = torch.cat([v[po:po + pl], v[so:so + ql]], 0)
+        mask = ref.causal_mask(ql, pl)
+        o = ref.attend(q[qs:qs + ql].transpose(0, 1)[None], kk.transpose(0, 1)[None], vv.transpose(0, 1)[None], mask)
+        out[qs:qs + ql] = o[0].transpose(0, 1)
+    return out
+
+
+def rand_attn(n_tok, n_kv, hq, hkv, D, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+
+    def rn(*s):
+        x = torch.randn(*s, generator=g)
+        return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dtype).to("cuda")
+
+    return rn(n_tok, hq, D), rn(n_kv, hkv, D), torch.randn(n_kv, hkv, D, generator=g).to(dtype).to("cuda")
+
+
+CASES = [
+    # (hq, hkv, D, segments (q_start, q_len, prefix_off, prefix_len, self_off), n_tok, n_kv)
+    (16, 8, 128, [(0, 64, 0, 2048, 2048), (64, 64, 0, 2048, 2112), (128, 64, 2176, 2048, 4224)], 192, 4288),
+    (2, 1, 128, [(0, 37, 0, 100, 300), (37, 150, 0, 100, 337), (187, 5, 100, 0, 487)], 192, 492),
+    (4, 1, 64, [(0, 70, 0, 513, 600), (70, 33, 513, 64, 670)], 103, 703),
+    (8, 2, 256, [(0, 48, 0, 300, 300), (48, 100, 0, 300, 348)], 148, 448),
+    (16, 4, 256, [(0, 128, 0, 1000, 1000)], 128, 1128),
+    (32, 8, 64, [(0, 64, 0, 700, 700), (64, 3, 0, 700, 764)], 67, 767),
+    (8, 8, 128, [(0, 200, 0, 0, 0)], 200, 200),
+]
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_attention_bf16_matches_oracle(case):
+    from cev_b200 import ops
+    hq, hkv, D, segs, n_tok, n_kv = CASES[case]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 100 + case)
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda")
+    out = ops.attend_packed(q, k, v, plan)
+    ops.device_status()
+    want = oracle_segments(q, k, v, segs)
+    rows = torch.zeros(n_tok, dtype=torch.bool)
+    for (qs, ql, *_r) in segs:
+        rows[qs:qs + ql] = True
+    err = (out.float().cpu()[rows] - want[rows]).abs().max().item()
+    assert err < BF16_TOL, err
+
+
+@pytest.mark.parametrize("case", [0, 1, 3])
+def test_attention_f32_matches_oracle(case):
+    from cev_b200 import ops
+    hq, hkv, D, segs, n_tok, n_kv = CASES[case]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.float32, 200 + case)
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.float32, "cuda")
+    out = ops.attend_packed(q, k, v, plan)
+    want = oracle_segments(q, k, v, segs)
+    rows = torch.zeros(n_tok, dtype=torch.bool)
+    for (qs, ql, *_r) in segs:
+        rows[qs:qs + ql] = True
+    assert (out.cpu()[rows] - want[rows]).abs().max().item() < F32_TOL
+
+
+def test_attention_repeatable_and_strided_q():
+    """Q read through a row stride (a view into a fused projection) gives
+    the same bits; two launches agree bit for bit."""
+    from cev_b200 import ops
+    hq, hkv, D, segs, n_tok, n_kv = CASES[0]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 7)
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda")
+    a = ops.attend_packed(q, k, v, plan)
+    wide = torch.zeros(n_tok, hq + 8, D, dtype=q.dtype, device="cuda")
+    wide[:, :hq] = q
+    b = ops.attend_packed(wide[:, :hq], k, v, plan)
+    c = ops.attend_packed(q, k, v, plan)
+    assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_attention_cfg2_shape_sampled():
+    """The cfg2 workload itself (32 requests x (2048 prefix + 16 x 64)),
+    checked against the oracle on a sample of requests."""
+    from cev_b200 import workloads
+    wb = workloads.AttentionBatch()
+    out = wb.run()
+    torch.cuda.synchronize()
+    from cev_b200 import ops
+    ops.device_status()
+    for rq in (0, 17, 31):
+        segs = [s for s in wb.segments if s[0] // 1024 == rq]
+        want = oracle_segments(wb.q, wb.k, wb.v, segs)
+        sl = slice(rq * 1024, (rq + 1) * 1024)
+        assert (out[sl].float().cpu() - want[sl]).abs().max().item() < BF16_TOL
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-5)])
+@pytest.mark.parametrize("plus_one,rot", [(False, 128), (True, 32), (False, 64)])
+def test_qk_norm_rope_matches_oracle(dtype, tol, plus_one, rot):
+    from cev_b200 import ops
+    torch.manual_seed(1)
+    T, hq, hkv, D = 37, 4, 2, 128
+    theta = 1e6
+    qkv = torch.randn(T, (hq + 2 * hkv) * D).to(dtype)
+    qw = (torch.rand(D) * 0.5 + 0.5).to(dtype)
+    kw = (torch.rand(D) * 0.5 + 0.5).to(dtype)
+    pos = torch.randint(0, 70000, (T,), dtype=torch.int32)
+    rows = torch.randperm(64)[:T].to(torch.int32)
+    qo = torch.empty(T, hq, D, dtype=dtype, device="cuda")
+    ka = torch.zeros(64, hkv, D, dtype=dtype, device="cuda")
+    va = torch.zeros(64, hkv, D, dtype=dtype, device="cuda")
+    ops.qk_norm_rope(qkv.cuda(), (0, D), hq * D, (hq + hkv) * D, hq, hkv, D, qw.cuda(), kw.cuda(), 1e-6, plus_one,
+                     pos.cuda(), theta, rot, qo, ka, va, rows.cuda())
+    wq = (qw.float() + 1).to(dtype) if plus_one else qw
+    wk = (kw.float() + 1).to(dtype) if plus_one else kw
+    x = qkv.float().reshape(T, hq + 2 * hkv, D)
+    cos, sin = ref.rope_cos_sin(pos.long(), rot, theta, torch.float32)
+    want_q = ref.rope_partial(ref.rms_norm(x[:, :hq].transpose(0, 1).to(dtype), wq, 1e-6).float(), cos, sin).transpose(0, 1)
+    want_k = ref.rope_partial(ref.rms_norm(x[:, hq:hq + hkv].transpose(0, 1).to(dtype), wk, 1e-6).float(), cos, sin).transpose(0, 1)
+    assert (qo.float().cpu() - want_q).abs().max().item() < tol
+    assert (ka.float().cpu()[rows.long()] - want_k).abs().max().item() < tol
+    assert torch.equal(va.cpu()[rows.long()], qkv.reshape(T, -1, D)[:, hq + hkv:])
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-5)])
+def test_norms_swiglu_embed_readout(dtype, tol):
+    from cev_b200 import ops
+    torch.manual_seed(2)
+    n, H, I = 9, 256, 512
+    x = torch.randn(n, H).to(dtype)
+    add = torch.randn(n, H).to(dtype)
+    w = (torch.rand(H) + 0.5).to(dtype)
+    out = ops.rms_norm(x.cuda(), w.cuda(), 1e-6)
+    assert (out.float().cpu() - ref.rms_norm(x, w, 1e-6).float()).abs().max().item() < tol
+    res = x.cuda().clone()
+    out = ops.add_rms_norm(res, add.cuda(), w.cuda(), 1e-6, plus_one=True)
+    s = (x + add)
+    assert (res.float().cpu() - s.float()).abs().max().item() < tol
+    assert (out.float().cpu() - ref.rms_norm(s, (w.float() + 1).to(dtype), 1e-6).float()).abs().max().item() < 3 * tol
+    gu = torch.randn(n, 2 * I).to(dtype)
+    y = ops.swiglu(gu.cuda())
+    assert (y.float().cpu() - (ref.silu(gu[:, :I].float()) * gu[:, I:].float())).abs().max().item() < 2 * tol
+    table = torch.randn(100, H).to(dtype)
+    ids = torch.randint(0, 100, (n,), dtype=torch.int32)
+    assert torch.equal(ops.embed(table.cuda(), ids.cuda()).cpu(), table[ids.long()])
+    head = torch.randn(5, H)
+    rows = torch.tensor([0, 4, 8], dtype=torch.int32)
+    hid, logits = ops.readout(x.cuda(), rows.cuda(), w.cuda(), 1e-6, False, head.cuda())
+    want_h = ref.rms_norm(x[rows.long()], w, 1e-6).float()
+    assert (hid.cpu() - want_h).abs().max().item() < tol
+    assert (logits.cpu() - want_h @ head.t()).abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 3e-2), (torch.float32, 1e-5)])
+@pytest.mark.parametrize("B,T,bcast", [(1, 50, False), (3, 7, True), (2, 1, False)])
+def test_short_conv_matches_oracle(dtype, tol, B, T, bcast):
+    """lfm2.rs:199-219 with a tail state (broadcast from one prefix or per row)."""
+    from cev_b200 import ops
+    torch.manual_seed(3)
+    d, K = 64, 3
+    bcx = torch.randn(B, T, 3 * d).to(dtype)
+    w = torch.randn(d, 1, K).to(dtype)
+    tail = torch.randn(1 if bcast else B, d, K - 1).to(dtype)
+    tail_out = torch.empty(B, d, K - 1, dtype=dtype, device="cuda")
+    y = ops.short_conv(bcx.reshape(B * T, 3 * d).cuda(), B, T, d, w.reshape(d, K).cuda(), None, tail.cuda(), tail_out)
+    bcu = bcx.transpose(1, 2)
+    bu = bcu[:, :d] * bcu[:, 2 * d:]
+    full = torch.cat([tail.expand(B, d, K - 1), bu], 2)
+    z = ref.depthwise_conv1d(full.float(), w.float())
+    want = (bcu[:, d:2 * d].float() * z).transpose(1, 2)
+    assert (y.float().cpu().reshape(B, T, d) - want).abs().max().item() < tol
+    assert (tail_out.float().cpu() - full[:, :, T:T + K - 1].float()).abs().max().item() < tol
+
+
+def gdn_inputs(B, T, nk, nv, dk, dv, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    C_ = 2 * nk * dk + nv * dv
+    conv_out = (torch.randn(B, T, C_, generator=g) * 0.5).to(dtype)
+    ab = torch.randn(B, T, 2 * nv, generator=g).to(dtype)
+    z = torch.randn(B, T, nv * dv, generator=g).to(dtype)
+    a_log = torch.rand(nv, generator=g) * 2
+    dt_bias = torch.rand(nv, generator=g)
+    norm_w = (torch.rand(dv, generator=g) + 0.5).to(dtype)
+    s0 = torch.randn(1, nv, dk, dv, generator=g) * 0.1
+    return conv_out, ab, z, a_log, dt_bias, norm_w, s0
+
+
+def gdn_oracle(conv_out, ab, z, a_log, dt_bias, norm_w, s0, nk, nv, dk, dv, eps=1e-6):
+    """qwen35.rs:432-451 after the conv, on CPU."""
+    B, T, _ = conv_out.shape
+    c = conv_out.float()
+    kd = nk * dk
+    q = c[..., :kd].reshape(B, T, nk, dk).transpose(1, 2)
+    k = c[..., kd:2 * kd].reshape(B, T, nk, dk).transpose(1, 2)
+    v = c[..., 2 * kd:].reshape(B, T, nv, dv).transpose(1, 2)
+    rep = nv // nk
+    q = q[:, :, None].expand(B, nk, rep, T, dk).reshape(B, nv, T, dk)
+    k = k[:, :, None].expand(B, nk, rep, T, dk).reshape(B, nv, T, dk)
+    beta = torch.sigmoid(ab[..., :nv].float()).transpose(1, 2)
+    g = (ref.softplus(ab[..., nv:].float() + dt_bias) * -a_log.exp()).transpose(1, 2)
+    core, s = ref.chunk_gated_delta_rule(q, k, v, g, beta, None if s0 is None else s0.expand(B, nv, dk, dv))
+    core = core.transpose(1, 2)
+    normed = core / (core.pow(2).mean(-1, keepdim=True) + eps).sqrt() * norm_w.float()
+    y = normed * ref.silu(z.float().reshape(B, T, nv, dv))
+    return y.reshape(B, T, nv * dv), s
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-4)])
+@pytest.mark.parametrize("B,T,with_state", [(1, 150, True), (3, 64, True), (2, 10, False)])
+def test_gdn_chunk_prefill_matches_oracle(dtype, tol, B, T, with_state):
+    from cev_b200 import ops
+    nk, nv, dk, dv = 2, 4, 64, 64
+    conv_out, ab, z, a_log, dt_bias, norm_w, s0 = gdn_inputs(B, T, nk, nv, dk, dv, dtype, 11)
+    s_in = s0.cuda() if with_state else None
+    s_out = torch.empty(B, nv, dk, dv, device="cuda")
+    ws = torch.empty(ops.gdn_workspace_size(B, T, nv, dk, dv), dtype=torch.uint8, device="cuda")
+    y = ops.gdn_chunk_prefill(conv_out.reshape(B * T, -1).cuda(), ab.reshape(B * T, -1).cuda(), 2 * nv,
+                              z.reshape(B * T, -1).cuda(), nv * dv, a_log.cuda(), dt_bias.cuda(), norm_w.cuda(), 1e-6,
+                              s_in, s_out, B, T, nk, nv, dk, dv, ws)
+    want_y, want_s = gdn_oracle(conv_out, ab, z, a_log, dt_bias, norm_w, s0 if with_state else None, nk, nv, dk, dv)
+    assert (y.float().cpu().reshape(B, T, -1) - want_y).abs().max().item() < tol
+    assert (s_out.cpu() - want_s).abs().max().item() < (tol if dtype == torch.float32 else 1e-3)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 3e-2), (torch.float32, 1e-5)])
+def test_gdn_conv_matches_oracle(dtype, tol):
+    from cev_b200 import ops
+    torch.manual_seed(4)
+    B, T, C_, K = 2, 9, 64, 4
+    mixed = torch.randn(B, T, C_ + 16).to(dtype)  # extra columns: a row stride
+    w = torch.randn(C_, 1, K).to(dtype)
+    tail = torch.randn(1, C_, K - 1).to(dtype)
+    tail_out = torch.empty(B, C_, K - 1, dtype=dtype, device="cuda")
+    y = ops.gdn_conv(mixed.reshape(B * T, -1).cuda(), B, T, C_, w.reshape(C_, K).cuda(), tail.cuda(), tail_out)
+    full = torch.cat([tail.expand(B, C_, K - 1), mixed[..., :C_].transpose(1, 2)], 2)
+    want = ref.silu(ref.depthwise_conv1d(full.float(), w.float())).transpose(1, 2)
+    assert (y.float().cpu().reshape(B, T, C_) - want).abs().max().item() < tol
+    assert torch.equal(tail_out.cpu(), full[:, :, T:T + K - 1].contiguous())
