@@ -176,7 +176,7 @@ def cpu_baseline_sample():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cevk")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -216,6 +216,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
+        time.sleep(1.0)  # let the sampler start before the timed region
         t_all0 = torch.cuda.Event(enable_timing=True)
         t_all1 = torch.cuda.Event(enable_timing=True)
         t_all0.record(stream)

@@ -114,8 +114,9 @@ int cevk_qk_norm_rope(const void* qkv, int32_t row_stride, int32_t q_head_stride
  * Token-wise RMSNorm (candle_nn::ops::rms_norm; qwen3.rs:254-255,
  * qwen35.rs:161-176 with plus_one, lfm2.rs operator/ffn norms).
  * If `residual` is non-NULL it is updated first: residual += add (the
- * decoder's `x = x + h`), then out = norm(residual).  x/add/out:
- * [n, hidden] contiguous.
+ * decoder's `x = x + h`), then out = norm(residual); with out == NULL only
+ * the residual add runs (w may then be NULL).  x/add/out: [n, hidden]
+ * contiguous.
  * ---------------------------------------------------------------------- */
 int cevk_rms_norm(const void* x, void* residual, const void* add, const void* w, void* out, int32_t n, int32_t hidden,
                   float eps, int32_t plus_one, int32_t dtype, void* stream);

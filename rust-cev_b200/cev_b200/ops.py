@@ -133,6 +133,14 @@ def add_rms_norm(residual: torch.Tensor, add: torch.Tensor, w: torch.Tensor, eps
     return out
 
 
+def residual_add(residual: torch.Tensor, add: torch.Tensor) -> torch.Tensor:
+    """residual += add in the model dtype (the decoder's ``x = x + h``)."""
+    _cuda(residual, add)
+    n, h = residual.shape
+    check(lib().cevk_rms_norm(None, _p(residual), _p(add), None, None, n, h, 0.0, 0, _dt(residual, add), _s()))
+    return residual
+
+
 def swiglu(gu: torch.Tensor, out=None) -> torch.Tensor:
     _cuda(gu)
     n, two_i = gu.shape

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
   }
+  if (!out) return;  // residual add only
   const float r = rsqrtf(block_sum(ss, red) / hidden + eps);
   for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
     float f[8], g[8];
@@ -187,7 +188,8 @@ extern "C" {
 
 int cevk_rms_norm(const void* x, void* residual, const void* add, const void* w, void* out, int32_t n, int32_t hidden,
                   float eps, int32_t plus_one, int32_t dtype, void* stream) {
-  if ((!x && !residual) || (residual && !add) || !w || !out) return set_error(CEVK_E_SHAPE, "rms_norm: null pointer");
+  if ((!x && !residual) || (residual && !add) || (out && !w) || (!out && !residual))
+    return set_error(CEVK_E_SHAPE, "rms_norm: null pointer");
   if (hidden % 8) return set_error(CEVK_E_SHAPE, "rms_norm: hidden %d not a multiple of 8", hidden);
   if (n <= 0) return CEVK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
