@@ -176,7 +176,7 @@ def cpu_baseline_sample():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--steps", type=int, default=600)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cevk")
     ap.add_argument("--no-cpu-baseline", action="store_true")

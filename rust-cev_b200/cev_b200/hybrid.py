@@ -1,0 +1,344 @@
+"""Recurrent-state decoders and the hybrid engine on the B200 kernels.
+
+Mirrors ``crates/cev-model/src/qwen35.rs`` (Gated DeltaNet + gated attention
+hybrid), ``crates/cev-model/src/lfm2.rs`` (gated short conv + GQA hybrid),
+``crates/cev-model/src/decoder.rs`` (``Decoder::forward``, ``PrefixState``)
+and the Codes path of ``crates/cev-model/src/hybrid.rs`` (prefix prefilled
+once in chunks into a cached state, then the questions as right-padded rows
+continuing it).
+
+State of a prefix (``PrefixState``, decoder.rs:54-105): the attention layers'
+K/V rows in the model's arena (one contiguous range shared by every
+attention layer), the GDN layers' conv tails and f32 recurrent matrices, and
+the short-conv layers' tails.  Rows continuing a state read it in place:
+attention through segment descriptors, GDN / conv through batch stride 0
+(the reference copies the state B times, decoder.rs:74-88).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .arena import KvArena, PrefixCache
+from .engine import InputError, Output, Readout, Request
+
+
+@dataclass
+class HybridState:
+    arena: KvArena | None
+    start: int
+    capacity: int
+    len: int = 0
+    next_pos: int = 0
+    gdn: dict = field(default_factory=dict)    # layer -> (conv tail [1,C,K-1], S [1,nv,dk,dv] f32)
+    conv: dict = field(default_factory=dict)   # layer -> tail [1,d,K-1]
+    pins: int = 0
+    released: bool = False
+
+    def release(self):
+        if not self.released and self.arena is not None and self.capacity > 0:
+            self.arena.release(self.start, self.capacity)
+        self.released = True
+        self.gdn, self.conv = {}, {}
+
+
+class _HybridDecoder:
+    """Shared layer loop of the two hybrid families."""
+
+    plus_one = False
+
+    def __init__(self, cfg, dtype, device, max_len, arena_rows):
+        self.cfg = cfg
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.hidden = cfg["hidden_size"]
+        self.hq = cfg["num_attention_heads"]
+        self.hkv = cfg["num_key_value_heads"]
+        self.D = cfg.get("head_dim") or self.hidden // self.hq
+        self.n_layers = cfg["num_hidden_layers"]
+        self.attn_layers = [i for i, t in enumerate(cfg["layer_types"]) if t == "full_attention"]
+        self.arena_index = {l: j for j, l in enumerate(self.attn_layers)}
+        self.arena = KvArena(len(self.attn_layers), arena_rows, self.hkv, self.D, dtype, self.device)
+        self.max_len = min(max_len, cfg.get("max_position_embeddings", max_len))
+
+    def _w(self, weights, name):
+        return weights[name].to(device=self.device, dtype=self.dtype)
+
+    def head_rows(self, ids) -> torch.Tensor:
+        return self.lm_head[torch.as_tensor(list(ids), dtype=torch.long, device=self.device)].float()
+
+    def new_state(self, n_tokens: int, cache=None) -> HybridState:
+        start = self.arena.alloc(n_tokens, cache) if self.attn_layers and n_tokens > 0 else 0
+        return HybridState(self.arena, start, n_tokens if self.attn_layers else 0)
+
+    def forward(self, tokens, B: int, T: int, pos, state: HybridState | None, keep: bool, cache=None):
+        """``Decoder::forward`` over B rows of T tokens (flattened,
+        row-major) at shared positions ``pos``, continuing ``state``.  With
+        ``keep`` (B == 1) the state is extended in place (its arena range
+        must have room).  Returns the residual stream [B*T, H] before the
+        final norm."""
+        if keep and B != 1:
+            raise ValueError("a prefix state is kept for one sequence at a time")
+        dev = self.device
+        n = B * T
+        ids = torch.tensor(tokens, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        pos_t = torch.tensor(list(pos) * B, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        past = 0 if state is None else state.len
+        scratch = None
+        if self.attn_layers:
+            if keep:
+                base = state.start + past
+                rows = list(range(base, base + T))
+                segs = [(0, T, state.start, past, base)]
+            else:
+                scratch = self.arena.alloc(n, cache)
+                rows = list(range(scratch, scratch + n))
+                pstart = 0 if state is None else state.start
+                segs = [(b * T, T, pstart, past, scratch + b * T) for b in range(B)]
+            rows_t = torch.tensor(rows, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            plan = ops.AttnPlan(segs, n, self.arena.capacity, self.hq, self.hkv, self.D, self.dtype, dev)
+        try:
+            x = ops.embed(self.embed_w, ids)
+            h = ops.rms_norm(x, self.layers[0]["ln1"], self.eps, self.plus_one)
+            m = None
+            for i, L in enumerate(self.layers):
+                if m is not None:
+                    h = ops.add_rms_norm(x, m, L["ln1"], self.eps, self.plus_one, out=h)
+                if L["kind"] == "attn":
+                    o = self._attn(i, L, h, pos_t, rows_t, plan)
+                elif L["kind"] == "gdn":
+                    o = self._gdn(i, L, h, B, T, state, keep)
+                else:
+                    o = self._conv(i, L, h, B, T, state, keep)
+                h = ops.add_rms_norm(x, o, L["ln2"], self.eps, self.plus_one, out=h)
+                m = F.linear(ops.swiglu(F.linear(h, L["gu"])), L["down"])
+            ops.residual_add(x, m)
+        finally:
+            if scratch is not None:
+                self.arena.release(scratch, n)
+        if keep:
+            state.len = past + T
+            state.next_pos = max(pos) + 1
+        return x
+
+    def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot):
+        T = h.shape[0]
+        hq, hkv, D = self.hq, self.hkv, self.D
+        qkv = F.linear(h, L["qkv"])
+        q = torch.empty(T, hq, D, dtype=self.dtype, device=self.device)
+        j = self.arena_index[i]
+        ops.qk_norm_rope(qkv, q_cols, k_col, v_col, hq, hkv, D, L["qn"], L["kn"], self.eps, self.plus_one, pos_t,
+                         self.theta, rot, q, self.arena.k[j], self.arena.v[j], rows_t)
+        return qkv, ops.attend_packed(q, self.arena.k[j], self.arena.v[j], plan)
+
+
+class Qwen35(_HybridDecoder):
+    """Qwen3.5 text decoder (qwen35.rs:625-752)."""
+
+    plus_one = True  # zero-centred RMSNorm (qwen35.rs:160-176)
+
+    def __init__(self, cfg: dict, weights: dict, dtype=torch.bfloat16, device="cuda", max_len=262144,
+                 arena_rows=65536 + 8192):
+        super().__init__(cfg, dtype, device, max_len, arena_rows)
+        self.eps = cfg.get("rms_norm_eps", 1e-6)
+        rp = cfg.get("rope_parameters") or {}
+        self.theta = rp.get("rope_theta") or cfg.get("rope_theta") or 1e7
+        self.rot = int(self.D * (rp.get("partial_rotary_factor") or 1.0)) & ~1
+        self.gate = cfg.get("attn_output_gate", True)
+        self.nk, self.nv = cfg["linear_num_key_heads"], cfg["linear_num_value_heads"]
+        self.dk, self.dv = cfg["linear_key_head_dim"], cfg["linear_value_head_dim"]
+        self.K = cfg.get("linear_conv_kernel_dim", 4)
+        self.C = 2 * self.nk * self.dk + self.nv * self.dv
+        w = lambda n: self._w(weights, n)  # noqa: E731
+        self.embed_w = w("model.embed_tokens.weight")
+        tied = cfg.get("tie_word_embeddings", False) or "lm_head.weight" not in weights
+        self.lm_head = self.embed_w if tied else w("lm_head.weight")
+        self.layers = []
+        for i in range(self.n_layers):
+            p = f"model.layers.{i}."
+            L = dict(ln1=w(p + "input_layernorm.weight"), ln2=w(p + "post_attention_layernorm.weight"),
+                     gu=torch.cat([w(p + "mlp.gate_proj.weight"), w(p + "mlp.up_proj.weight")], 0).contiguous(),
+                     down=w(p + "mlp.down_proj.weight"))
+            if cfg["layer_types"][i] == "linear_attention":
+                a = p + "linear_attn."
+                L.update(kind="gdn",
+                         proj=torch.cat([w(a + "in_proj_qkv.weight"), w(a + "in_proj_z.weight"),
+                                         w(a + "in_proj_b.weight"), w(a + "in_proj_a.weight")], 0).contiguous(),
+                         conv_w=w(a + "conv1d.weight").reshape(self.C, self.K).contiguous(),
+                         a_log=weights[a + "A_log"].to(self.device, torch.float32),
+                         dt_bias=weights[a + "dt_bias"].to(self.device, torch.float32),
+                         norm_w=w(a + "norm.weight"), out=w(a + "out_proj.weight"))
+            else:
+                s = p + "self_attn."
+                L.update(kind="attn",
+                         qkv=torch.cat([w(s + "q_proj.weight"), w(s + "k_proj.weight"), w(s + "v_proj.weight")],
+                                       0).contiguous(),
+                         qn=w(s + "q_norm.weight"), kn=w(s + "k_norm.weight"), o=w(s + "o_proj.weight"))
+            self.layers.append(L)
+        self.norm_w = w("model.norm.weight")
+
+    def _attn(self, i, L, h, pos_t, rows_t, plan):
+        """qwen35.rs:526-560: q|gate per head, (1+w) QK-norm, partial RoPE,
+        sigmoid output gate."""
+        hq, hkv, D = self.hq, self.hkv, self.D
+        qw = 2 * D if self.gate else D
+        qkv, ctx = self._attn_common(i, L, h, pos_t, rows_t, plan, (0, qw), hq * qw, hq * qw + hkv * D, self.rot)
+        T = h.shape[0]
+        out = ctx.view(T, hq * D)
+        if self.gate:
+            ops.sigmoid_gate(out, qkv[:, D:], qkv.stride(0), 2 * D, hq, D)
+        return F.linear(out, L["o"])
+
+    def _gdn(self, i, L, h, B, T, state, keep):
+        """GatedDeltaNet::forward (qwen35.rs:415-453)."""
+        nk, nv, dk, dv, C, K = self.nk, self.nv, self.dk, self.dv, self.C, self.K
+        proj = F.linear(h, L["proj"])
+        prev = None if state is None else state.gdn.get(i)
+        tail_in = None if prev is None else prev[0]
+        s_in = None if prev is None else prev[1]
+        tail_out = torch.empty(1, C, K - 1, dtype=self.dtype, device=self.device) if keep else None
+        s_out = torch.empty(1, nv, dk, dv, dtype=torch.float32, device=self.device) if keep else None
+        conv_out = ops.gdn_conv(proj, B, T, C, L["conv_w"], tail_in, tail_out)
+        ws = torch.empty(ops.gdn_workspace_size(B, T, nv, dk, dv), dtype=torch.uint8, device=self.device)
+        y = ops.gdn_chunk_prefill(conv_out, proj[:, C + nv * dv:], proj.stride(0), proj[:, C:], proj.stride(0),
+                                  L["a_log"], L["dt_bias"], L["norm_w"], self.eps, s_in, s_out, B, T, nk, nv, dk, dv,
+                                  ws)
+        if keep:
+            state.gdn[i] = (tail_out, s_out)
+        return F.linear(y, L["out"])
+
+
+class Lfm2(_HybridDecoder):
+    """LFM2 causal decoder (lfm2.rs:270-431)."""
+
+    def __init__(self, cfg: dict, weights: dict, dtype=torch.bfloat16, device="cuda", max_len=128000,
+                 arena_rows=65536 + 8192):
+        super().__init__(cfg, dtype, device, max_len, arena_rows)
+        self.eps = cfg.get("norm_eps", 1e-5)
+        self.theta = cfg.get("rope_theta") or (cfg.get("rope_parameters") or {}).get("rope_theta") or 1e6
+        self.K = cfg.get("conv_L_cache", 3)
+        w = lambda n: self._w(weights, n)  # noqa: E731
+        self.embed_w = w("model.embed_tokens.weight")
+        self.lm_head = self.embed_w
+        self.layers = []
+        d = self.hidden
+        for i in range(self.n_layers):
+            p = f"model.layers.{i}."
+            f = p + "feed_forward."
+            L = dict(ln1=w(p + "operator_norm.weight"), ln2=w(p + "ffn_norm.weight"),
+                     gu=torch.cat([w(f + "w1.weight"), w(f + "w3.weight")], 0).contiguous(), down=w(f + "w2.weight"))
+            if cfg["layer_types"][i] == "full_attention":
+                s = p + "self_attn."
+                L.update(kind="attn",
+                         qkv=torch.cat([w(s + "q_proj.weight"), w(s + "k_proj.weight"), w(s + "v_proj.weight")],
+                                       0).contiguous(),
+                         qn=w(s + "q_layernorm.weight"), kn=w(s + "k_layernorm.weight"), o=w(s + "out_proj.weight"))
+            else:
+                c = p + "conv."
+                L.update(kind="conv", in_proj=w(c + "in_proj.weight"), out=w(c + "out_proj.weight"),
+                         conv_w=w(c + "conv.weight").reshape(d, self.K).contiguous(),
+                         bias=w(c + "conv.bias") if (c + "conv.bias") in weights else None)
+            self.layers.append(L)
+        self.norm_w = w("model.embedding_norm.weight")
+
+    def _attn(self, i, L, h, pos_t, rows_t, plan):
+        """lfm2.rs:145-171."""
+        hq, hkv, D = self.hq, self.hkv, self.D
+        _, ctx = self._attn_common(i, L, h, pos_t, rows_t, plan, (0, D), hq * D, (hq + hkv) * D, D)
+        return F.linear(ctx.view(h.shape[0], hq * D), L["o"])
+
+    def _conv(self, i, L, h, B, T, state, keep):
+        """ShortConv::forward (lfm2.rs:199-219)."""
+        d, K = self.hidden, self.K
+        bcx = F.linear(h, L["in_proj"])
+        tail_in = None if state is None else state.conv.get(i)
+        tail_out = torch.empty(1, d, K - 1, dtype=self.dtype, device=self.device) if keep else None
+        y = ops.short_conv(bcx, B, T, d, L["conv_w"], L["bias"], tail_in, tail_out)
+        if keep:
+            state.conv[i] = tail_out
+        return F.linear(y, L["out"])
+
+
+class HybridEngine:
+    """Codes readout of the hybrid engine (hybrid.rs:155-165, 454-772)."""
+
+    def __init__(self, decoder: _HybridDecoder, code_ids, pad_id: int, prefill_chunk=512, pass_tokens=2048,
+                 prefix_cache_tokens=65536):
+        self.decoder = decoder
+        self.head = decoder.head_rows(code_ids).contiguous()
+        self.pad_id = pad_id
+        self.prefill_chunk = prefill_chunk
+        self.pass_tokens = pass_tokens
+        self.cache = PrefixCache(prefix_cache_tokens)
+
+    def prefill(self, prefix) -> HybridState:
+        """The prefix in chunks into a state, cached (hybrid.rs:555-575)."""
+        chunk = max(self.prefill_chunk, 1)
+        st = self.decoder.new_state(len(prefix), self.cache)
+        st.pins += 1
+        try:
+            done = 0
+            while done < len(prefix):
+                n = min(chunk, len(prefix) - done)
+                self.decoder.forward(prefix[done:done + n], 1, n, range(done, done + n), st, True, self.cache)
+                done += n
+        except BaseException:
+            st.pins -= 1
+            st.release()
+            raise
+        return st
+
+    def rows(self, state: HybridState, rows) -> torch.Tensor:
+        """A right-padded batch continuing ``state`` (hybrid.rs:595-617);
+        returns the residual stream [B*T, H]."""
+        t = max(len(r) for r in rows)
+        ids = []
+        for r in rows:
+            ids += list(r) + [self.pad_id] * (t - len(r))
+        pos = range(state.next_pos, state.next_pos + t)
+        return self.decoder.forward(ids, len(rows), t, pos, state, False, self.cache), t
+
+    def run(self, req: Request) -> Output:
+        """hybrid.rs:697-739 with the Codes readout of 619-641."""
+        d = self.decoder
+        if len(req.prefix) == 0:
+            raise InputError("empty shared prefix")
+        longest = max(len(req.prefix) + len(s) for s in req.suffixes)
+        if longest >= d.max_len:
+            raise InputError(f"prompt is {longest} tokens; the context limit is {d.max_len}")
+        state = self.cache.get(req.prefix)
+        cached = state is not None
+        if cached:
+            state.pins += 1
+        else:
+            state = self.prefill(list(req.prefix))
+        try:
+            readouts, start, br = [], 0, req.suffixes
+            while start < len(br):
+                end, longest = start + 1, len(br[start])
+                while end < len(br):
+                    l = max(longest, len(br[end]))
+                    if l * (end + 1 - start) > self.pass_tokens:
+                        break
+                    longest = l
+                    end += 1
+                rows = br[start:end]
+                x, t = self.rows(state, rows)
+                g = torch.tensor([i * t + len(r) - 1 for i, r in enumerate(rows)], dtype=torch.int32)
+                hid, logits = ops.readout(x, g.to(d.device), d.norm_w, d.eps, d.plus_one, self.head)
+                hid, logits = hid.cpu(), logits.cpu()
+                for i, r in enumerate(rows):
+                    k = req.n_options[start + i]
+                    readouts.append(Readout(logits[i, :k].clone(), hid[i].clone()))
+                start = end
+        finally:
+            state.pins -= 1
+            if not cached and not self.cache.put(list(req.prefix), state) and not state.pins:
+                state.release()
+        return Output(readouts, len(req.prefix) + sum(len(s) for s in req.suffixes), cached)
+
+    def run_many(self, reqs):
+        return [self.run(r) for r in reqs]

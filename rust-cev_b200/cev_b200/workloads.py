@@ -78,3 +78,43 @@ class AttentionBatch:
         request's K/V rows once."""
         e = self.q.element_size()
         return e * (2 * self.q.numel() + self.k.numel() + self.v.numel())
+
+
+# ---------------------------------------------------------------------------
+# Decision requests at the token-id level.
+# ---------------------------------------------------------------------------
+CODE_BASE = 100  # code j ("A", "B", ...) is token CODE_BASE + j in the synthetic vocabularies
+SEP_ID = 13
+
+
+def make_questions(gen: torch.Generator, n_q: int, lengths, n_opt: int, vocab: int):
+    """``n_q`` questions whose rendered suffix has exactly the drawn length:
+    head, ``n_opt`` x (code, separator, option ids), tail."""
+    from .service import Question
+    qs = []
+    for i in range(n_q):
+        total = int(lengths[i])
+        body = total - 2 * n_opt
+        opt_len = max(1, body // (2 * n_opt))
+        head = max(1, (body - n_opt * opt_len) // 2)
+        tail = body - n_opt * opt_len - head
+        assert tail >= 1, (total, n_opt)
+
+        def ids(n):
+            return torch.randint(200, vocab, (n,), generator=gen).tolist()
+
+        qs.append(Question(ids(head), [ids(opt_len) for _ in range(n_opt)], ids(tail)))
+    return qs
+
+
+def code_ids(n: int):
+    return [CODE_BASE + j for j in range(n)]
+
+
+def decision_request(seed: int, prefix_len: int, n_q: int, len_lo: int, len_hi: int, n_opt: int, vocab: int):
+    """A seeded request: (prefix ids, questions).  Prefix ids are uniform in
+    [0, vocab); question lengths uniform in [len_lo, len_hi]."""
+    gen = torch.Generator().manual_seed(seed)
+    prefix = torch.randint(0, vocab, (prefix_len,), generator=gen).tolist()
+    lengths = torch.randint(len_lo, len_hi + 1, (n_q,), generator=gen).tolist()
+    return prefix, make_questions(gen, n_q, lengths, n_opt, vocab)

@@ -231,6 +231,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     float s[BN];
+    uint32_t pk[BN / 2];
     for (int j = 0; j < n_blk; ++j) {
       if (!mbar_wait(b_sfull(j & 1), (j >> 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
@@ -238,56 +239,70 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
 #pragma unroll
       for (int c = 0; c < BN; c += 32) tmem_ld32(sc + c, s + c);
       tmem_wait_ld();
-      // Validity of key column c: prefix block -> inside the prefix;
-      // own block -> causal.
-      int lim;
-      if (j < n_pre) lim = seg.prefix_len - j * BN - 1;
-      else lim = t - (j - n_pre) * BN;
-      float mb = -INFINITY;
+      // Key column c is visible if c <= lim: inside the prefix for a prefix
+      // block, causal for an own block.  Full blocks skip the mask.
+      const int lim = (j < n_pre) ? seg.prefix_len - j * BN - 1 : t - (j - n_pre) * BN;
+      if (lim < BN - 1) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        s[c] = (c <= lim) ? s[c] * p.scale_log2 : -INFINITY;
-        mb = fmaxf(mb, s[c]);
+        for (int c = 0; c < BN; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
       }
+      // Row max of the raw scores (scale > 0 commutes with max): 8
+      // independent chains, then a tree.
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < BN; c += 8)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], s[c + i]);
+      const float mb = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * p.scale_log2;
+      // Rescale only when the running max grows by more than 2^8.
+      const bool need = (j == 0) || (mb > m_run + 8.f);
+      const float m_new = need ? mb : m_run;
+      const float factor = (j > 0 && need) ? fast_exp2(m_run - m_new) : 1.f;
+      // P = 2^(s*scale - m): one FFMA + one ex2 per element, computed while
+      // the previous block's PV is still on the tensor cores.
+      const float neg = -m_new;
+      float sm8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sm8[i] = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const float e0 = fast_exp2(fmaf(s[c], p.scale_log2, neg));
+        const float e1 = fast_exp2(fmaf(s[c + 1], p.scale_log2, neg));
+        sm8[c & 7] += e0;
+        sm8[(c + 1) & 7] += e1;
+        pk[c >> 1] = pack_bf16x2(e0, e1);
+      }
+      const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
       if (j > 0) {
         // PV of the previous block must be done: P smem is reused and O may
         // be rescaled.
         if (!mbar_wait(b_odone, (j - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const bool need = mb > m_run + 8.f;
-        if (__any_sync(0xffffffffu, need)) {
-          const float f = need ? fast_exp2(m_run - mb) : 1.f;
+        if (__any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             float o[32];
             tmem_ld32(tl + C::TM_O + c, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= f;
+            for (int i = 0; i < 32; ++i) o[i] *= factor;
             tmem_st32(tl + C::TM_O + c, o);
           }
           tmem_wait_st();
         }
-        if (need) { l_run *= fast_exp2(m_run - mb); m_run = mb; }
-      } else {
-        m_run = mb;
       }
-      float sum = 0.f;
+      l_run = l_run * factor + sum;
+      m_run = m_new;
       uint8_t* prow = smem + C::OFF_P + (r * 128);
 #pragma unroll
       for (int c = 0; c < BN; c += 8) {
-        float e[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { e[i] = fast_exp2(s[c + i] - m_run); sum += e[i]; }
-        uint4 pk;
-        pk.x = pack_bf16x2(e[0], e[1]);
-        pk.y = pack_bf16x2(e[2], e[3]);
-        pk.z = pack_bf16x2(e[4], e[5]);
-        pk.w = pack_bf16x2(e[6], e[7]);
+        const uint4 v = make_uint4(pk[c >> 1], pk[(c >> 1) + 1], pk[(c >> 1) + 2], pk[(c >> 1) + 3]);
         const int atom = c >> 6, chunk = (c & 63) >> 3;
-        *reinterpret_cast<uint4*>(prow + atom * C::ATOM + ((chunk ^ (r & 7)) << 4)) = pk;
+        *reinterpret_cast<uint4*>(prow + atom * C::ATOM + ((chunk ^ (r & 7)) << 4)) = v;
       }
-      l_run += sum;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(b_pfull);

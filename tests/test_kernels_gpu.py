@@ -194,7 +194,7 @@ def test_norms_swiglu_embed_readout(dtype, tol):
     assert close(gated, want.reshape(n, -1), tol, rel)
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 3e-2), (torch.float32, 1e-5)])
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 1e-2), (torch.float32, 1e-5)])
 @pytest.mark.parametrize("B,T,bcast", [(1, 50, False), (3, 7, True), (2, 1, False)])
 def test_short_conv_matches_oracle(dtype, tol, B, T, bcast):
     """lfm2.rs:199-219 with a tail state (broadcast from one prefix or per row)."""
@@ -211,8 +211,9 @@ def test_short_conv_matches_oracle(dtype, tol, B, T, bcast):
     full = torch.cat([tail.expand(B, d, K - 1), bu], 2)
     z = ref.depthwise_conv1d(full.float(), w.float())
     want = (bcu[:, d:2 * d].float() * z).transpose(1, 2)
-    assert (y.float().cpu().reshape(B, T, d) - want).abs().max().item() < tol
-    assert (tail_out.float().cpu() - full[:, :, T:T + K - 1].float()).abs().max().item() < tol
+    rel = dtype == torch.bfloat16
+    assert close(y.reshape(B, T, d), want, tol, rel)
+    assert close(tail_out, full[:, :, T:T + K - 1], tol, rel)
 
 
 def gdn_inputs(B, T, nk, nv, dk, dv, dtype, seed):
@@ -261,11 +262,13 @@ def test_gdn_chunk_prefill_matches_oracle(dtype, tol, B, T, with_state):
                               z.reshape(B * T, -1).cuda(), nv * dv, a_log.cuda(), dt_bias.cuda(), norm_w.cuda(), 1e-6,
                               s_in, s_out, B, T, nk, nv, dk, dv, ws)
     want_y, want_s = gdn_oracle(conv_out, ab, z, a_log, dt_bias, norm_w, s0 if with_state else None, nk, nv, dk, dv)
-    assert (y.float().cpu().reshape(B, T, -1) - want_y).abs().max().item() < tol
-    assert (s_out.cpu() - want_s).abs().max().item() < (tol if dtype == torch.float32 else 1e-3)
+    # bf16: y is rounded once to bf16 at the end; the core runs in f32
+    rel = dtype == torch.bfloat16
+    assert close(y.reshape(B, T, -1), want_y, 1e-2 if rel else tol, rel)
+    assert close(s_out, want_s, 1e-3 if rel else tol, rel)
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 3e-2), (torch.float32, 1e-5)])
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 1e-2), (torch.float32, 1e-5)])
 def test_gdn_conv_matches_oracle(dtype, tol):
     from cev_b200 import ops
     torch.manual_seed(4)
@@ -277,5 +280,5 @@ def test_gdn_conv_matches_oracle(dtype, tol):
     y = ops.gdn_conv(mixed.reshape(B * T, -1).cuda(), B, T, C_, w.reshape(C_, K).cuda(), tail.cuda(), tail_out)
     full = torch.cat([tail.expand(B, C_, K - 1), mixed[..., :C_].transpose(1, 2)], 2)
     want = ref.silu(ref.depthwise_conv1d(full.float(), w.float())).transpose(1, 2)
-    assert (y.float().cpu().reshape(B, T, C_) - want).abs().max().item() < tol
+    assert close(y.reshape(B, T, C_), want, tol, dtype == torch.bfloat16)
     assert torch.equal(tail_out.cpu(), full[:, :, T:T + K - 1].contiguous())

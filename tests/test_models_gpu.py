@@ -1,0 +1,114 @@
+"""Model- and engine-level parity on the GPU against the CPU oracle: the
+packed block-mask Qwen3 engine, the Qwen3.5 and LFM2 hybrid engines, and the
+debiased served probabilities, on seeded random-init weights and seeded
+token ids.  Served probabilities: |dp| < 5e-5 in f32 and < 1e-3 in bf16."""
+import pytest
+import torch
+
+from cev_b200 import configs, weights, workloads
+from oracle import engine as oeng
+from oracle import hybrid as ohyb
+from oracle import qwen3 as oq3
+from oracle import service as osvc
+
+pytestmark = pytest.mark.gpu
+
+
+def to_oracle_q(qs):
+    return [osvc.Question(q.head, q.options, q.tail, list(q.order)) for q in qs]
+
+
+def rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_qwen3_engine_passes_tails_cache_match_oracle(dtype):
+    from cev_b200.engine import Engine, Request
+    from cev_b200.qwen3 import Qwen3
+    cfg = configs.tiny_qwen3()
+    w = weights.init_weights(cfg, 21)
+    codes = workloads.code_ids(4)
+    gpu = Engine(Qwen3(cfg, w, dtype, "cuda", arena_rows=4096), codes, prefill_chunk=48, pass_tokens=96)
+    ref = oeng.Engine(oq3.Qwen3(cfg, w), codes, prefill_chunk=48, pass_tokens=96)
+    prefix, qs = workloads.decision_request(5, 150, 5, 20, 40, 4, cfg["vocab_size"])
+    sfx = [q.render(codes, workloads.SEP_ID) for q in qs]
+    req = Request(prefix, sfx, [4] * len(sfx))
+    a = gpu.run(req)
+    b = ref.run(oeng.Request(prefix, sfx, [4] * len(sfx)))
+    assert not a.prefix_cached
+    tol = 1e-4 if dtype == torch.float32 else 3e-2
+    for x, y in zip(a.readouts, b.readouts):
+        assert rel(x.hidden, y.hidden) < tol
+        assert (x.logits - y.logits).abs().max().item() < tol
+    again = gpu.run(req)
+    assert again.prefix_cached
+    for x, y in zip(a.readouts, again.readouts):
+        assert (x.logits - y.logits).abs().max().item() < (1e-4 if dtype == torch.float32 else 2e-2)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 5e-5), (torch.bfloat16, 1e-3)])
+def test_served_probabilities_full_debias_match_oracle(dtype, tol):
+    """run_debiased with rotations and a content-free calibration twin fused
+    into the same run_many (service.rs:288-348)."""
+    from cev_b200 import service
+    from cev_b200.engine import Engine
+    from cev_b200.qwen3 import Qwen3
+    cfg = configs.tiny_qwen3()
+    w = weights.init_weights(cfg, 22)
+    codes = workloads.code_ids(3)
+    prefix, qs = workloads.decision_request(6, 100, 4, 30, 30, 3, cfg["vocab_size"])
+    cf = [7, 8, 9, 10, 11]
+    gpu = Engine(Qwen3(cfg, w, dtype, "cuda", arena_rows=4096), codes, prefill_chunk=64)
+    ref = oeng.Engine(oq3.Qwen3(cfg, w), codes, prefill_chunk=64)
+    _, p_gpu = service.run_debiased(gpu, prefix, qs, "full", codes, workloads.SEP_ID, cf)
+    _, p_ref = osvc.run_debiased(ref, prefix, to_oracle_q(qs), "full", codes, workloads.SEP_ID, cf)
+    worst = max(abs(a - b) for pa, pb in zip(p_gpu, p_ref) for a, b in zip(pa, pb))
+    assert worst < tol, worst
+
+
+@pytest.mark.parametrize("family", ["qwen35", "lfm2"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_hybrid_engine_matches_oracle(family, dtype):
+    from cev_b200 import hybrid
+    from cev_b200.engine import Request
+    cfg = configs.tiny_qwen35() if family == "qwen35" else configs.tiny_lfm2()
+    w = weights.init_weights(cfg, 31)
+    codes = workloads.code_ids(3)
+    dec = (hybrid.Qwen35 if family == "qwen35" else hybrid.Lfm2)(cfg, w, dtype, "cuda", arena_rows=4096)
+    odec = (ohyb.Qwen35 if family == "qwen35" else ohyb.Lfm2)(cfg, w)
+    gpu = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=64, pass_tokens=80)
+    ref = ohyb.HybridEngine(odec, codes, pad_id=0, prefill_chunk=64, pass_tokens=80)
+    prefix, qs = workloads.decision_request(7, 150, 5, 12, 30, 3, cfg["vocab_size"])
+    sfx = [q.render(codes, workloads.SEP_ID) for q in qs]
+    a = gpu.run(Request(prefix, sfx, [3] * len(sfx)))
+    b = ref.run(oeng.Request(prefix, sfx, [3] * len(sfx)))
+    tol = 2e-4 if dtype == torch.float32 else 3e-2
+    for x, y in zip(a.readouts, b.readouts):
+        assert rel(x.hidden, y.hidden) < tol
+        assert (x.logits - y.logits).abs().max().item() < tol
+    again = gpu.run(Request(prefix, sfx, [3] * len(sfx)))
+    assert again.prefix_cached and not a.prefix_cached
+    for x, y in zip(a.readouts, again.readouts):
+        assert (x.logits - y.logits).abs().max().item() < 1e-4
+
+
+def test_cfg1_full_pipeline_f32_served_probabilities():
+    """cfg1: Qwen3-0.6B-shaped, seed 0, f32, one request (256-token state,
+    4 questions of 48 tokens, 3 codes, 3 rotations + calibration twin) in
+    one packed pass; served probabilities within 5e-5 of the oracle."""
+    from cev_b200 import service
+    from cev_b200.engine import Engine
+    from cev_b200.qwen3 import Qwen3
+    cfg = configs.get("cfg1")
+    w = weights.init_weights(cfg, 0)
+    codes = workloads.code_ids(3)
+    prefix, qs = workloads.decision_request(0, 256, 4, 48, 48, 3, 151643)
+    cf = [11, 12, 13, 14]
+    gpu = Engine(Qwen3(cfg, w, torch.float32, "cuda", arena_rows=2048), codes, pass_tokens=4096)
+    _, p_gpu = service.run_debiased(gpu, prefix, qs, "full", codes, workloads.SEP_ID, cf)
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref = oeng.Engine(oq3.Qwen3(cfg, w), codes, pass_tokens=4096)
+    _, p_ref = osvc.run_debiased(ref, prefix, to_oracle_q(qs), "full", codes, workloads.SEP_ID, cf)
+    worst = max(abs(a - b) for pa, pb in zip(p_gpu, p_ref) for a, b in zip(pa, pb))
+    assert worst < 5e-5, worst
