@@ -55,8 +55,8 @@ class KvArena:
     """Per-layer K and V row storage for the attention layers of a model."""
 
     def __init__(self, n_layers: int, capacity: int, kv_heads: int, head_dim: int, dtype, device):
-        self.k = [torch.empty(capacity, kv_heads, head_dim, dtype=dtype, device=device) for _ in range(n_layers)]
-        self.v = [torch.empty(capacity, kv_heads, head_dim, dtype=dtype, device=device) for _ in range(n_layers)]
+        self.k = [torch.zeros(capacity, kv_heads, head_dim, dtype=dtype, device=device) for _ in range(n_layers)]
+        self.v = [torch.zeros(capacity, kv_heads, head_dim, dtype=dtype, device=device) for _ in range(n_layers)]
         self.rows = RowAllocator(capacity)
         self.capacity = capacity
 

@@ -296,6 +296,23 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
       l_run = l_run * factor + sum;
       m_run = m_new;
+      // Key rows past the tile's last visible key carry P = 0, but their V
+      // rows are whatever the buffer holds there (possibly NaN/Inf, and
+      // 0 * NaN = NaN in the MMA): zero them before PV reads the stage.
+      {
+        const int vcount = (j < n_pre) ? seg.prefix_len - j * BN : (t0 + nt) - (j - n_pre) * BN;
+        if (vcount < BN) {
+          const int vst = j % KST;
+          if (!mbar_wait(b_vfull(vst), (j / KST) & 1, abort_flag)) { ok = false; break; }
+          const int rows0 = vcount < 0 ? 0 : vcount;
+          const int chunks = (BN - rows0) * 8 * (D / 64);
+          uint8_t* vb = smem + C::OFF_V + vst * C::KV_BYTES;
+          for (int i = threadIdx.x - 128; i < chunks; i += 128) {
+            const int a = i / ((BN - rows0) * 8), rem = i % ((BN - rows0) * 8);
+            *reinterpret_cast<uint4*>(vb + a * BN * 128 + (rows0 + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
       uint8_t* prow = smem + C::OFF_P + (r * 128);
 #pragma unroll
       for (int c = 0; c < BN; c += 8) {

@@ -86,6 +86,29 @@ def test_attention_f32_matches_oracle(case):
     assert (out.cpu()[rows] - want[rows]).abs().max().item() < F32_TOL
 
 
+@pytest.mark.parametrize("case", [1, 2, 5])
+def test_attention_ignores_nonfinite_rows_outside_segments(case):
+    """Rows of K/V outside every segment's visible range may hold anything
+    (NaN/Inf garbage of an uninitialised arena): outputs stay exact."""
+    from cev_b200 import ops
+    hq, hkv, D, segs, n_tok, n_kv = CASES[case]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 300 + case)
+    used = torch.zeros(n_kv, dtype=torch.bool)
+    for (qs, ql, po, pl, so) in segs:
+        used[po:po + pl] = True
+        used[so:so + ql] = True
+    k2, v2 = k.clone(), v.clone()
+    k2[~used.cuda()] = float("nan")
+    v2[~used.cuda()] = float("inf")
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda")
+    a = ops.attend_packed(q, k, v, plan)
+    b = ops.attend_packed(q, k2, v2, plan)
+    rows = torch.zeros(n_tok, dtype=torch.bool)
+    for (qs, ql, *_r) in segs:
+        rows[qs:qs + ql] = True
+    assert torch.equal(a[rows.cuda()], b[rows.cuda()])
+
+
 def test_attention_repeatable_and_strided_q():
     """Q read through a row stride (a view into a fused projection) gives
     the same bits; two launches agree bit for bit."""
