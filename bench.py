@@ -173,6 +173,49 @@ def cpu_baseline_sample():
             "sample": f"1 request prefix + {n_suf} suffixes, f32 torch CPU, {reps} reps over ~10 s"}
 
 
+def decisions_bench(n_req: int, dev, world: int, dist_mod):
+    """cfg3: Qwen3-8B-shaped decoder (bf16, random init seed 1); per request
+    an 8192-token random-id state (head 7680 prefilled in 512-token chunks,
+    tail 512 in the packed pass) and 32 questions of U[48,128] tokens with 4
+    option codes x 2 rotations, all 64 suffixes in one packed pass; served
+    probabilities on the host.  Decisions = questions answered.  Timed end to
+    end per request: token ids in from the host, probabilities out."""
+    import torch
+    from cev_b200 import configs, service, weights, workloads
+    from cev_b200.engine import Engine
+    from cev_b200.qwen3 import Qwen3
+    cfg = configs.get("cfg3")
+    w = weights.init_weights(cfg, 1, torch.bfloat16, dev)
+    model = Qwen3(cfg, w, torch.bfloat16, dev, arena_rows=65536 + 16384)
+    del w
+    codes = workloads.code_ids(4)
+    eng = Engine(model, codes, prefill_chunk=512, pass_tokens=16384)
+    rank = int(os.environ.get("RANK", "0"))
+    reqs = [workloads.decision_request(10_000 * (rank + 1) + i, 8192, 32, 48, 128, 4, 151643) for i in range(n_req + 1)]
+
+    def one(prefix, qs):
+        return service.run_debiased(eng, prefix, qs, "permute", codes, workloads.SEP_ID, max_permutations=2)
+
+    one(*reqs[0])  # warm-up (distinct prefix: no cache hit later)
+    eng.cache.clear()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist_mod.barrier()
+    t0 = time.perf_counter()
+    for prefix, qs in reqs[1:]:
+        _, probs = one(prefix, qs)
+        assert len(probs) == 32
+    torch.cuda.synchronize()
+    dt = torch.tensor([time.perf_counter() - t0], device=dev)
+    if world > 1:
+        dist_mod.all_reduce(dt, op=dist_mod.ReduceOp.MAX)
+    n_dec = 32 * n_req * world
+    flop = 7.47e12 * n_dec
+    return {"value": n_dec / dt.item(), "unit": "decisions/s", "requests_per_gpu": n_req,
+            "seconds": dt.item(), "workload": "cfg3 Qwen3-8B-shaped bf16, 8192-token state, 32 questions x 2 rotations",
+            "approx_tflops": flop / dt.item() / 1e12}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -180,6 +223,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cevk")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decisions", type=int, default=0,
+                    help="also measure cfg3 decisions/sec on this many requests per GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -299,6 +344,10 @@ def main():
         "clocks": clk.summary(),
         "gpu_launches": args.steps,
     }
+    if args.decisions > 0:
+        del wb, dq, dk, dv, do, hq_, hk, hv, ho
+        torch.cuda.empty_cache()
+        line["decisions"] = decisions_bench(args.decisions, dev, world, dist)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:

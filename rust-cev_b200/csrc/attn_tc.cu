@@ -17,10 +17,11 @@
 //             (TMEM lane = row).
 // TMEM: two S buffers (BN columns each, f32) so QK^T of block j+1 runs
 // while block j is in softmax, and the O accumulator (D columns, f32).
-// P (bf16) goes through shared memory in the 128B-swizzled K-major layout
-// the UMMA descriptor reads.  Online softmax in the log2 domain; O is only
-// rescaled when a row max grows by more than 2^8 (values of P stay <= 256,
-// exact in f32 accumulation), which keeps TMEM traffic off the common path.
+// P (bf16) overwrites its own S in TMEM and feeds the PV UMMA as the TMEM A
+// operand, so the softmax never waits for the previous PV (only an O
+// rescale does).  Online softmax in the log2 domain; O is only rescaled when
+// a row max grows by more than 2^8 (values of P stay <= 256, exact in f32
+// accumulation), which keeps TMEM traffic off the common path.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -36,12 +37,10 @@ struct AttnTc {
   static constexpr int ATOM = BM * 128;         // one 64-column (128 B) slab of a 128-row tile
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + KST * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int OFF_BAR = OFF_V + KST * KV_BYTES;
   // barriers: q_full, k_full[KST], k_empty[KST], v_full[KST], v_empty[KST],
   // s_full[2], p_full, o_done, drain
   static constexpr int N_BAR = 1 + 4 * KST + 2 + 3;
@@ -55,7 +54,7 @@ struct AttnTc {
   // one CTA's softmax then overlaps the other's UMMAs.
   static constexpr int MIN_BLOCKS = (2 * (SMEM + 1024) <= 233472 && TM_COLS <= 256) ? 2 : 1;
   static_assert(D % 64 == 0 && BN % 64 == 0 && BN <= 128, "tile shape");
-  static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_P % 1024 == 0, "1024-aligned tiles");
+  static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0, "1024-aligned tiles");
 };
 
 struct AttnParams {
@@ -89,7 +88,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     if (threadIdx.x == 0) atomicExch(&g_device_error, kErrWaitTimeout);
     return;
   }
-  const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V, sP = sbase + C::OFF_P;
+  const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
   const uint32_t bar0 = sbase + C::OFF_BAR;
   const uint32_t b_qfull = bar0;
   auto b_kfull = [&](int s) { return bar0 + 8u * (1 + s); };
@@ -207,11 +206,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       if (!mbar_wait(b_vfull(st), (j / KST) & 1, abort_flag)) break;
       tc_fence_after();
       const uint32_t vb = sV + st * C::KV_BYTES;
+      // P_j (bf16) sits in the first BN/2 columns of S_j's buffer.
+      const uint32_t pa = tmem + ((j & 1) ? C::TM_S1 : C::TM_S0);
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk) {
-        const uint64_t ad = umma_desc_sw128(sP + (kk >> 2) * C::ATOM + (kk & 3) * 32, 16, 1024);
         const uint64_t bd = umma_desc_sw128(vb + kk * 16 * 128, BN * 128, 1024);
-        umma_bf16_ss(tmem + C::TM_O, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_bf16_ts(tmem + C::TM_O, pa + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
       }
       umma_commit(b_odone);
       umma_commit(b_vempty(st));
@@ -276,12 +276,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         pk[c >> 1] = pack_bf16x2(e0, e1);
       }
       const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
-      if (j > 0) {
-        // PV of the previous block must be done: P smem is reused and O may
-        // be rescaled.
+      if (__any_sync(0xffffffffu, factor != 1.f)) {
+        // O is rescaled in TMEM: PV of the previous block must be done (and
+        // PV of this block cannot start before P_j is signalled).
         if (!mbar_wait(b_odone, (j - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, factor != 1.f)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             float o[32];
@@ -311,16 +311,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             const int a = i / ((BN - rows0) * 8), rem = i % ((BN - rows0) * 8);
             *reinterpret_cast<uint4*>(vb + a * BN * 128 + (rows0 + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
           }
+          fence_proxy_async_smem();
         }
       }
-      uint8_t* prow = smem + C::OFF_P + (r * 128);
+      // P_j overwrites the (already read) S_j in TMEM, packed bf16x2.
 #pragma unroll
-      for (int c = 0; c < BN; c += 8) {
-        const uint4 v = make_uint4(pk[c >> 1], pk[(c >> 1) + 1], pk[(c >> 1) + 2], pk[(c >> 1) + 3]);
-        const int atom = c >> 6, chunk = (c & 63) >> 3;
-        *reinterpret_cast<uint4*>(prow + atom * C::ATOM + ((chunk ^ (r & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
+      for (int c = 0; c < BN / 2; c += 32) tmem_st32(sc + c, reinterpret_cast<const float*>(pk + c));
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(b_pfull);
     }

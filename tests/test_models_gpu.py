@@ -76,17 +76,22 @@ def test_hybrid_engine_matches_oracle(family, dtype):
     w = weights.init_weights(cfg, 31)
     codes = workloads.code_ids(3)
     dec = (hybrid.Qwen35 if family == "qwen35" else hybrid.Lfm2)(cfg, w, dtype, "cuda", arena_rows=4096)
-    odec = (ohyb.Qwen35 if family == "qwen35" else ohyb.Lfm2)(cfg, w)
+    # bf16 runs are held to the oracle run with the same model dtype (its
+    # matmuls and stored activations rounded to bf16, like candle's).
+    odec = (ohyb.Qwen35 if family == "qwen35" else ohyb.Lfm2)(cfg, w, dtype)
     gpu = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=64, pass_tokens=80)
     ref = ohyb.HybridEngine(odec, codes, pad_id=0, prefill_chunk=64, pass_tokens=80)
     prefix, qs = workloads.decision_request(7, 150, 5, 12, 30, 3, cfg["vocab_size"])
     sfx = [q.render(codes, workloads.SEP_ID) for q in qs]
     a = gpu.run(Request(prefix, sfx, [3] * len(sfx)))
     b = ref.run(oeng.Request(prefix, sfx, [3] * len(sfx)))
-    tol = 2e-4 if dtype == torch.float32 else 3e-2
+    tol = 2e-4 if dtype == torch.float32 else 5e-2
     for x, y in zip(a.readouts, b.readouts):
         assert rel(x.hidden, y.hidden) < tol
         assert (x.logits - y.logits).abs().max().item() < tol
+        if dtype == torch.bfloat16:
+            pa, pb = torch.softmax(x.logits.double(), 0), torch.softmax(y.logits.double(), 0)
+            assert (pa - pb).abs().max().item() < 1e-2
     again = gpu.run(Request(prefix, sfx, [3] * len(sfx)))
     assert again.prefix_cached and not a.prefix_cached
     for x, y in zip(a.readouts, again.readouts):
