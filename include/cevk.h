@@ -186,6 +186,29 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
                            int32_t T, int32_t nk, int32_t nv, int32_t dk, int32_t dv, void* workspace,
                            size_t workspace_bytes, int32_t dtype, void* stream);
 
+/* Allocation-free variant of cevk_gdn_chunk_prefill (no counterpart in the
+ * reference).  For callers that cannot give this library a workspace: hosts
+ * whose device memory belongs to their own fixed pool, or paths where a
+ * cudaMalloc is not allowed or would stall.  Same arguments and results as
+ * cevk_gdn_chunk_prefill without workspace / workspace_bytes; the f32
+ * scratch is a fixed device array inside the library (CEVK_GDN_NOALLOC_MAX_BYTES,
+ * held by every GPU that loads the library until exit).
+ *   - Calls needing more scratch (B*T*nv*dv*4 bytes) than the array holds
+ *     return CEVK_E_SHAPE; split them or use the workspace entry point.
+ *   - The first call on a device looks up the array's device address (once
+ *     per device, with that device current); make that first call before
+ *     any stream capture.
+ *   - Allocates nothing: no cudaMalloc / cudaFree or allocating library call.
+ *   - All calls share the array: calls that overlap on the GPU (other
+ *     streams, other host threads on the same device) race.  Nothing in it
+ *     needs to start at zero; each call overwrites what it reads. */
+#define CEVK_GDN_NOALLOC_MAX_BYTES ((size_t)16 << 20)
+int cevk_gdn_chunk_prefill_noalloc(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride,
+                                   const void* z, int32_t z_row_stride, const float* a_log, const float* dt_bias,
+                                   const void* norm_w, float eps, const float* s_in, int64_t s_batch_stride,
+                                   float* s_out, void* y, int32_t B, int32_t T, int32_t nk, int32_t nv, int32_t dk,
+                                   int32_t dv, int32_t dtype, void* stream);
+
 /* ------------------------------------------------------------------------
  * LFM2 gated short convolution (ShortConv::forward, lfm2.rs:199-219):
  * y = C (.) conv_K(B (.) X) continuing from a tail of K-1 inputs.

@@ -39,6 +39,7 @@ SIGNATURES = {
     "cevk_gdn_conv": (C.c_int, [P, I32, P, P, I64, P, P, I32, I32, I32, I32, I32, P]),
     "cevk_gdn_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "cevk_gdn_chunk_prefill": (C.c_int, [P, I32, P, I32, P, I32, P, P, P, F, P, I64, P, P, I32, I32, I32, I32, I32, I32, P, SZ, I32, P]),
+    "cevk_gdn_chunk_prefill_noalloc": (C.c_int, [P, I32, P, I32, P, I32, P, P, P, F, P, I64, P, P, I32, I32, I32, I32, I32, I32, I32, P]),
     "cevk_short_conv": (C.c_int, [P, P, P, P, I64, P, P, I32, I32, I32, I32, I32, P]),
 }
 

@@ -339,3 +339,64 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of cevk_gdn_chunk_prefill.
+//
+// Some hosts cannot hand this library a workspace: their device memory is
+// owned by a fixed pool of their own (an embedding runtime that only gives
+// out its tensors), or they run the decision forward on a path where a
+// cudaMalloc is not allowed or would stall it.  For them the f32 scratch of
+// the chunked delta rule lives in a fixed device array in this file.  Every
+// GPU that loads the library holds the array until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace cevk {
+
+constexpr size_t kGdnStaticScratchBytes = CEVK_GDN_NOALLOC_MAX_BYTES;
+static __device__ __align__(256) float g_gdn_scratch[kGdnStaticScratchBytes / sizeof(float)];
+
+// Device address of g_gdn_scratch for the current device, looked up once per
+// device (the host-side name is only a stand-in, not a device address).
+static int gdn_static_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[128] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "gdn noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128) return set_error(CEVK_E_CUDA, "gdn noalloc: device ordinal %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gdn_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(CEVK_E_CUDA, "gdn noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return CEVK_OK;
+}
+
+}  // namespace cevk
+
+extern "C" int cevk_gdn_chunk_prefill_noalloc(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride,
+                                              const void* z, int32_t z_row_stride, const float* a_log,
+                                              const float* dt_bias, const void* norm_w, float eps, const float* s_in,
+                                              int64_t s_batch_stride, float* s_out, void* y, int32_t B, int32_t T,
+                                              int32_t nk, int32_t nv, int32_t dk, int32_t dv, int32_t dtype,
+                                              void* stream) {
+  if (B <= 0 || T <= 0) return CEVK_OK;
+  const size_t need = cevk_gdn_workspace_size(B, T, nv, dk, dv);
+  if (need > cevk::kGdnStaticScratchBytes)
+    return cevk::set_error(CEVK_E_SHAPE,
+                           "gdn noalloc: %d rows x %d tokens x %d heads x %d columns need %zu bytes of scratch, "
+                           "over the %zu-byte static array; split the call or use cevk_gdn_chunk_prefill",
+                           B, T, nv, dv, need, cevk::kGdnStaticScratchBytes);
+  float* ws = nullptr;
+  const int rc = cevk::gdn_static_scratch(&ws);
+  if (rc) return rc;
+  return cevk_gdn_chunk_prefill(conv_out, C, ab, ab_row_stride, z, z_row_stride, a_log, dt_bias, norm_w, eps, s_in,
+                                s_batch_stride, s_out, y, B, T, nk, nv, dk, dv, ws, cevk::kGdnStaticScratchBytes, dtype,
+                                stream);
+}
