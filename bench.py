@@ -216,6 +216,47 @@ def decisions_bench(n_req: int, dev, world: int, dist_mod):
             "approx_tflops": flop / dt.item() / 1e12}
 
 
+def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
+    """cfg4 (Qwen3.5-shaped GDN hybrid, seed 2, 16384-token state, 32
+    questions of U[32,128] tokens) or cfg5 (LFM2-shaped, seed 3, 65536-token
+    state in 512-token chunks, 64 questions of 64 tokens): the state is
+    prefilled once into the cached prefix state, the questions run as
+    right-padded rows continuing it (hybrid.rs:697-739).  4 option codes,
+    2 rotations per question (cfg4) / none (cfg5).  Decisions/s end to end."""
+    import torch
+    from cev_b200 import configs, hybrid, service, weights, workloads
+    cfg = configs.get(name)
+    seed, plen, nq, lo, hi, mode = (2, 16384, 32, 32, 128, "permute") if name == "cfg4" else (3, 65536, 64, 64, 64, "none")
+    w = weights.init_weights(cfg, seed, torch.bfloat16, dev)
+    dec = (hybrid.Qwen35 if name == "cfg4" else hybrid.Lfm2)(cfg, w, torch.bfloat16, dev, max_len=plen + 1024,
+                                                             arena_rows=plen + 8192)
+    del w
+    codes = workloads.code_ids(4)
+    eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=512, pass_tokens=8192, prefix_cache_tokens=plen)
+    rank = int(os.environ.get("RANK", "0"))
+    vocab = cfg["vocab_size"] - 1
+    reqs = [workloads.decision_request(20_000 * (rank + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]
+
+    def one(prefix, qs):
+        return service.run_debiased(eng, prefix, qs, mode, codes, workloads.SEP_ID, max_permutations=2)
+
+    one(*reqs[0])
+    eng.cache.clear()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist_mod.barrier()
+    t0 = time.perf_counter()
+    for prefix, qs in reqs[1:]:
+        _, probs = one(prefix, qs)
+        assert len(probs) == nq
+    torch.cuda.synchronize()
+    dt = torch.tensor([time.perf_counter() - t0], device=dev)
+    if world > 1:
+        dist_mod.all_reduce(dt, op=dist_mod.ReduceOp.MAX)
+    return {"value": nq * n_req * world / dt.item(), "unit": "decisions/s", "requests_per_gpu": n_req,
+            "seconds": dt.item(), "workload": f"{name}: {plen}-token state, {nq} questions, rows continuing the state"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -223,8 +264,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cevk")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--decisions", type=int, default=0,
-                    help="also measure cfg3 decisions/sec on this many requests per GPU")
+    ap.add_argument("--decisions", type=int, default=4,
+                    help="also measure cfg3 decisions/sec on this many requests per GPU (0 = skip)")
+    ap.add_argument("--hybrid", type=int, default=0,
+                    help="also measure cfg4 and cfg5 decisions/sec on this many requests per GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -344,10 +387,16 @@ def main():
         "clocks": clk.summary(),
         "gpu_launches": args.steps,
     }
-    if args.decisions > 0:
+    if args.decisions > 0 or args.hybrid > 0:
         del wb, dq, dk, dv, do, hq_, hk, hv, ho
         torch.cuda.empty_cache()
+    if args.decisions > 0:
         line["decisions"] = decisions_bench(args.decisions, dev, world, dist)
+        torch.cuda.empty_cache()
+    if args.hybrid > 0:
+        for name in ("cfg4", "cfg5"):
+            line[f"decisions_{name}"] = hybrid_decisions_bench(name, args.hybrid, dev, world, dist)
+            torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:

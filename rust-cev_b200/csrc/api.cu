@@ -10,6 +10,9 @@
 namespace cevk {
 
 __device__ int g_device_error = 0;
+__device__ int g_device_error_info[4] = {0, 0, 0, 0};
+__device__ int g_device_error_n = 0;
+__device__ int g_device_error_more[64];
 
 static thread_local char g_msg[512] = "";
 
@@ -50,7 +53,25 @@ int cevk_device_status(void) {
   if (cudaMemcpyFromSymbol(&flag, g_device_error, sizeof(int)) != cudaSuccess ||
       cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess)
     return set_error(CEVK_E_CUDA, "cannot read the device error flag");
-  if (flag) return set_error(CEVK_E_TIMEOUT, "a bounded device wait gave up (code %d)", flag);
+  if (flag) {
+    int info[4] = {0, 0, 0, 0}, zeros[4] = {0, 0, 0, 0};
+    cudaMemcpyFromSymbol(info, g_device_error_info, sizeof(info));
+    cudaMemcpyToSymbol(g_device_error_info, zeros, sizeof(zeros));
+    int n = 0, more[64];
+    cudaMemcpyFromSymbol(&n, g_device_error_n, sizeof(int));
+    cudaMemcpyFromSymbol(more, g_device_error_more, sizeof(more));
+    cudaMemcpyToSymbol(g_device_error_n, zeros, sizeof(int));
+    char extra[384] = "";
+    int len = 0;
+    for (int i = 0; i < n && i < 16 && len < 320; ++i)
+      if (more[4 * i] == info[0])
+        len += snprintf(extra + len, sizeof(extra) - len, " [t%d 0x%x p%d]", more[4 * i + 1], more[4 * i + 2],
+                        more[4 * i + 3]);
+    return set_error(CEVK_E_TIMEOUT,
+                     "a bounded device wait gave up (code %d): block %d thread %d barrier smem offset 0x%x parity %d;"
+                     " also stopped in that block:%s",
+                     flag, info[0], info[1], info[2], info[3], extra);
+  }
   return CEVK_OK;
 }
 

@@ -1,22 +1,24 @@
 // Packed block-masked prefill attention on sm_100a tensor cores.
 //
-// One CTA computes one work tile: 128 query rows of one segment and one KV
-// head -- the G = hq/hkv query heads of that KV head times 128/G tokens,
-// row r <-> (token t0 + r/G, head r%G) -- so every K/V tile it loads serves
-// all G heads (GQA without copies).  The tile walks the segment's visible
-// keys only: the prefix range (full) and its own rows (causal, only up to
-// the tile's last token).  Key tiles of other segments are never loaded,
-// and no mask is materialised: validity is decided per element from the
-// segment descriptor.
+// A work tile is 128 query rows of one segment and one KV head -- the
+// G = hq/hkv query heads of that KV head times 128/G tokens, row r <->
+// (token t0 + r/G, head r%G) -- so every K/V tile loaded serves all G heads
+// (GQA without copies).  A tile walks the segment's visible keys only: the
+// prefix range (full) and its own rows (causal, only up to the tile's last
+// token).  Key tiles of other segments are never loaded, and no mask is
+// materialised: validity is decided per element from the segment descriptor.
 //
-// Warp roles (256 threads):
-//   warp 0  TMA producer for Q and K (one elected lane)
-//   warp 1  TMEM allocator + UMMA issuer (one elected lane)
-//   warp 2  TMA producer for V
-//   warps 4-7  softmax / O correction / epilogue, one query row per thread
-//             (TMEM lane = row).
-// TMEM: two S buffers (BN columns each, f32) so QK^T of block j+1 runs
-// while block j is in softmax, and the O accumulator (D columns, f32).
+// A CTA runs NT = 2 work tiles (1 for head_dim 256) in ping-pong: one UMMA
+// issuer alternates strictly between the tiles, so while one tile's softmax
+// runs, the tensor cores work on the other tile's QK^T and PV.
+// Warp roles (416 threads for NT = 2):
+//   warps 0 / 3   TMA producers for Q and K of tile 0 / 1 (one elected lane)
+//   warps 2 / 12  TMA producers for V of tile 0 / 1
+//   warp 1        TMEM allocator + UMMA issuer (one elected lane)
+//   warps 4-7 / 8-11  softmax / O correction / epilogue of tile 0 / 1, one
+//                 query row per thread (TMEM lane = row).
+// TMEM per tile: two S buffers (BN f32 columns each) so QK^T of block j+1
+// runs while block j is in softmax, and the O accumulator (D f32 columns).
 // P (bf16) overwrites its own S in TMEM and feeds the PV UMMA as the TMEM A
 // operand, so the softmax never waits for the previous PV (only an O
 // rescale does).  Online softmax in the log2 domain; O is only rescaled when
@@ -31,36 +33,45 @@
 
 namespace cevk {
 
-template <int D, int BN, int KST>
+template <int D, int BN, int KSK, int KSV, int NT>
 struct AttnTc {
   static constexpr int BM = 128;
   static constexpr int ATOM = BM * 128;         // one 64-column (128 B) slab of a 128-row tile
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + KST * KV_BYTES;
-  // barriers: q_full, k_full[KST], k_empty[KST], v_full[KST], v_empty[KST],
-  // s_full[2], p_full, o_done, drain
-  static constexpr int N_BAR = 1 + 4 * KST + 2 + 3;
-  static constexpr int OFF_MISC = OFF_BAR + N_BAR * 8;
+  // per work tile: Q, K ring, V ring
+  static constexpr int T_OFF_Q = 0;
+  static constexpr int T_OFF_K = Q_BYTES;
+  static constexpr int T_OFF_V = T_OFF_K + KSK * KV_BYTES;
+  static constexpr int T_BYTES = T_OFF_V + KSV * KV_BYTES;
+  // barriers per tile: q_full, k_full[KSK], k_empty[KSK], v_full[KSV],
+  // v_empty[KSV], s_full, s_free, p_full[2], o_done[2] (by block parity).
+  // A parity wait cannot tell phase k from k+2, so every waiter must be at
+  // most one phase away from its barrier; the comments at each wait say why.
+  static constexpr int T_BARS = 1 + 2 * KSK + 2 * KSV + 6;
+  static constexpr int OFF_BAR = NT * T_BYTES;
+  static constexpr int OFF_MISC = OFF_BAR + (NT * T_BARS + 1) * 8;  // + drain
   static constexpr int SMEM = OFF_MISC + 16;
-  static constexpr int TM_S0 = 0;
-  static constexpr int TM_S1 = BN;
+  // TMEM per tile: S (BN f32 columns), P double buffer (BN/2 columns of
+  // packed bf16 each), O (D f32 columns).
+  static constexpr int TM_S = 0;
+  static constexpr int TM_P = BN;
   static constexpr int TM_O = 2 * BN;
-  static constexpr int TM_COLS = (2 * BN + D) <= 256 ? 256 : 512;
-  // Two CTAs per SM when both fit (228 KB per SM, 1 KB reserved per CTA):
-  // one CTA's softmax then overlaps the other's UMMAs.
-  static constexpr int MIN_BLOCKS = (2 * (SMEM + 1024) <= 233472 && TM_COLS <= 256) ? 2 : 1;
+  static constexpr int TM_TILE = 256;           // TMEM columns per tile
+  static constexpr int TM_COLS = NT == 1 && (2 * BN + D) <= 256 ? 256 : 512;
+  static constexpr int THREADS = NT == 2 ? 416 : 256;
+  static constexpr int MIN_BLOCKS = (NT == 1 && TM_COLS <= 256 && 2 * (OFF_MISC + 16 + 1024) <= 233472) ? 2 : 1;
+  static_assert(2 * BN + D <= 512 / NT, "TMEM budget");
   static_assert(D % 64 == 0 && BN % 64 == 0 && BN <= 128, "tile shape");
-  static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0, "1024-aligned tiles");
+  static_assert(T_OFF_K % 1024 == 0 && T_OFF_V % 1024 == 0 && T_BYTES % 1024 == 0, "1024-aligned tiles");
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 struct AttnParams {
   __nv_bfloat16* o;
   const cevk_segment* segs;
   int n_segs;
+  int n_work;  // work tiles = segment tiles x KV heads
   int hq, hkv, group, rows_t;
   int o_row_stride;
   float scale_log2;
@@ -75,11 +86,38 @@ __device__ __forceinline__ int find_segment(const cevk_segment* segs, int n, int
   return lo;
 }
 
-template <int D, int BN, int KST>
-__global__ void __launch_bounds__(256, AttnTc<D, BN, KST>::MIN_BLOCKS)
+// One work tile: 128 query rows (G heads x 128/G tokens) of one segment and
+// one KV head, and the key blocks it walks.
+struct Work {
+  cevk_segment seg;
+  int kvh, t0, nt, n_pre, n_blk;
+  __device__ __forceinline__ int kv_row(int j, int BN) const {
+    return j < n_pre ? seg.prefix_off + j * BN : seg.self_off + (j - n_pre) * BN;
+  }
+};
+
+__device__ __forceinline__ Work decode_work(const AttnParams& p, int w, int BN) {
+  Work k;
+  if (w >= p.n_work) {
+    k.n_blk = 0;
+    k.nt = 0;
+    return k;
+  }
+  const int tile = w / p.hkv;
+  k.kvh = w % p.hkv;
+  k.seg = p.segs[find_segment(p.segs, p.n_segs, tile)];
+  k.t0 = (tile - k.seg.tile_start) * p.rows_t;
+  k.nt = min(p.rows_t, k.seg.q_len - k.t0);
+  k.n_pre = (k.seg.prefix_len + BN - 1) / BN;
+  k.n_blk = k.n_pre + (k.t0 + k.nt + BN - 1) / BN;
+  return k;
+}
+
+template <int D, int BN, int KSK, int KSV, int NT>
+__global__ void __launch_bounds__(AttnTc<D, BN, KSK, KSV, NT>::THREADS, AttnTc<D, BN, KSK, KSV, NT>::MIN_BLOCKS)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, AttnParams p) {
-  using C = AttnTc<D, BN, KST>;
+  using C = AttnTc<D, BN, KSK, KSV, NT>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   // The swizzled tiles need a 1024-byte aligned base (no static shared
@@ -88,46 +126,44 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     if (threadIdx.x == 0) atomicExch(&g_device_error, kErrWaitTimeout);
     return;
   }
-  const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
-  const uint32_t bar0 = sbase + C::OFF_BAR;
-  const uint32_t b_qfull = bar0;
-  auto b_kfull = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto b_kempty = [&](int s) { return bar0 + 8u * (1 + KST + s); };
-  auto b_vfull = [&](int s) { return bar0 + 8u * (1 + 2 * KST + s); };
-  auto b_vempty = [&](int s) { return bar0 + 8u * (1 + 3 * KST + s); };
-  auto b_sfull = [&](int s) { return bar0 + 8u * (1 + 4 * KST + s); };
-  const uint32_t b_pfull = bar0 + 8u * (3 + 4 * KST);
-  const uint32_t b_odone = bar0 + 8u * (4 + 4 * KST);
-  const uint32_t b_drain = bar0 + 8u * (5 + 4 * KST);
+  auto sQ = [&](int t) { return sbase + t * C::T_BYTES + C::T_OFF_Q; };
+  auto sK = [&](int t, int st) { return sbase + t * C::T_BYTES + C::T_OFF_K + st * C::KV_BYTES; };
+  auto sV = [&](int t, int st) { return sbase + t * C::T_BYTES + C::T_OFF_V + st * C::KV_BYTES; };
+  auto bar = [&](int t, int i) { return sbase + C::OFF_BAR + 8u * (t * C::T_BARS + i); };
+  auto b_qfull = [&](int t) { return bar(t, 0); };
+  constexpr int KV4 = 2 * KSK + 2 * KSV;
+  auto b_kfull = [&](int t, int s) { return bar(t, 1 + s); };
+  auto b_kempty = [&](int t, int s) { return bar(t, 1 + KSK + s); };
+  auto b_vfull = [&](int t, int s) { return bar(t, 1 + 2 * KSK + s); };
+  auto b_vempty = [&](int t, int s) { return bar(t, 1 + 2 * KSK + KSV + s); };
+  auto b_sfull = [&](int t) { return bar(t, 1 + KV4); };
+  auto b_sfree = [&](int t) { return bar(t, 2 + KV4); };
+  auto b_pfull = [&](int t, int s) { return bar(t, 3 + KV4 + s); };
+  auto b_odone = [&](int t, int s) { return bar(t, 5 + KV4 + s); };
+  const uint32_t b_drain = sbase + C::OFF_BAR + 8u * (NT * C::T_BARS);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // ---- work decode (every thread; cheap) ----
-  const int tile = blockIdx.x / p.hkv;
-  const int kvh = blockIdx.x % p.hkv;
-  const int si = find_segment(p.segs, p.n_segs, tile);
-  const cevk_segment seg = p.segs[si];
-  const int t0 = (tile - seg.tile_start) * p.rows_t;
-  const int nt = min(p.rows_t, seg.q_len - t0);
-  const int n_pre = (seg.prefix_len + BN - 1) / BN;
-  const int n_self = (t0 + nt + BN - 1) / BN;
-  const int n_blk = n_pre + n_self;
-  auto kv_row = [&](int j) { return j < n_pre ? seg.prefix_off + j * BN : seg.self_off + (j - n_pre) * BN; };
-
   if (threadIdx.x == 0) {
-    mbar_init(b_qfull, 1);
-    for (int s = 0; s < KST; ++s) {
-      mbar_init(b_kfull(s), 1);
-      mbar_init(b_kempty(s), 1);
-      mbar_init(b_vfull(s), 1);
-      mbar_init(b_vempty(s), 1);
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(b_qfull(t), 1);
+      for (int s = 0; s < KSK; ++s) {
+        mbar_init(b_kfull(t, s), 1);
+        mbar_init(b_kempty(t, s), 1);
+      }
+      for (int s = 0; s < KSV; ++s) {
+        mbar_init(b_vfull(t, s), 1);
+        mbar_init(b_vempty(t, s), 1);
+      }
+      mbar_init(b_sfull(t), 1);
+      mbar_init(b_sfree(t), 128);
+      mbar_init(b_pfull(t, 0), 128);
+      mbar_init(b_pfull(t, 1), 128);
+      mbar_init(b_odone(t, 0), 1);
+      mbar_init(b_odone(t, 1), 1);
     }
-    mbar_init(b_sfull(0), 1);
-    mbar_init(b_sfull(1), 1);
-    mbar_init(b_pfull, 128);
-    mbar_init(b_odone, 1);
     mbar_init(b_drain, 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -141,107 +177,151 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- Q + K producer ----------------
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    mbar_arrive_expect_tx(b_qfull, C::Q_BYTES);
-#pragma unroll
-    for (int a = 0; a < D / 64; ++a) tma_load_3d(sQ + a * C::ATOM, &tm_q, b_qfull, a * 64, kvh * p.group, seg.q_start + t0);
-    int issued = 0;
-    for (int j = 0; j < n_blk; ++j) {
-      const int st = j % KST;
-      if (j >= KST && !mbar_wait(b_kempty(st), ((j / KST) - 1) & 1, abort_flag)) break;
-      mbar_arrive_expect_tx(b_kfull(st), C::KV_BYTES);
-#pragma unroll
-      for (int a = 0; a < D / 64; ++a) tma_load_3d(sK + st * C::KV_BYTES + a * BN * 128, &tm_k, b_kfull(st), a * 64, kvh, kv_row(j));
-      issued = j + 1;
-    }
-    // Drain: the last load of every stage has landed before the CTA exits.
+  // Roles: warp 0 / 3 load Q and K of tile 0 / 1, warp 2 / 12 load V of
+  // tile 0 / 1, warp 1 issues UMMAs, warps 4-7 / 8-11 run tile 0 / 1's softmax.
+  const int qk_tile = warp == 0 ? 0 : (NT == 2 && warp == 3 ? 1 : -1);
+  const int v_tile = warp == 2 ? 0 : (NT == 2 && warp == 12 ? 1 : -1);
+
+  if (qk_tile >= 0 && lane == 0) {
+    // ---------------- Q + K producer of one tile ----------------
+    const int t = qk_tile;
+    const Work wk = decode_work(p, blockIdx.x * NT + t, BN);
     volatile int never = 0;
-    mbar_wait(b_qfull, 0, &never, 1ll << 30);
-    for (int j = max(0, issued - KST); j < issued; ++j) mbar_wait(b_kfull(j % KST), (j / KST) & 1, &never, 1ll << 30);
-  } else if (warp == 2 && lane == 0) {
-    // ---------------- V producer ----------------
-    tma_prefetch_desc(&tm_v);
-    int issued = 0;
-    for (int j = 0; j < n_blk; ++j) {
-      const int st = j % KST;
-      if (j >= KST && !mbar_wait(b_vempty(st), ((j / KST) - 1) & 1, abort_flag)) break;
-      mbar_arrive_expect_tx(b_vfull(st), C::KV_BYTES);
+    if (wk.n_blk > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      mbar_arrive_expect_tx(b_qfull(t), C::Q_BYTES);
 #pragma unroll
-      for (int a = 0; a < D / 64; ++a) tma_load_3d(sV + st * C::KV_BYTES + a * BN * 128, &tm_v, b_vfull(st), a * 64, kvh, kv_row(j));
-      issued = j + 1;
+      for (int a = 0; a < D / 64; ++a)
+        tma_load_3d(sQ(t) + a * C::ATOM, &tm_q, b_qfull(t), a * 64, wk.kvh * p.group, wk.seg.q_start + wk.t0);
+      int issued = 0;
+      for (int j = 0; j < wk.n_blk; ++j) {
+        const int st = j % KSK;
+        if (j >= KSK && !mbar_wait(b_kempty(t, st), ((j / KSK) - 1) & 1, abort_flag)) break;
+        mbar_arrive_expect_tx(b_kfull(t, st), C::KV_BYTES);
+#pragma unroll
+        for (int a = 0; a < D / 64; ++a)
+          tma_load_3d(sK(t, st) + a * BN * 128, &tm_k, b_kfull(t, st), a * 64, wk.kvh, wk.kv_row(j, BN));
+        issued = j + 1;
+      }
+      // Drain: the Q load and the last load of every stage have landed.
+      mbar_wait(b_qfull(t), 0, &never, 1ll << 30);
+      for (int j = max(0, issued - KSK); j < issued; ++j)
+        mbar_wait(b_kfull(t, j % KSK), (j / KSK) & 1, &never, 1ll << 30);
     }
-    for (int j = max(0, issued - KST); j < issued; ++j) {
-      volatile int never = 0;
-      mbar_wait(b_vfull(j % KST), (j / KST) & 1, &never, 1ll << 30);
+  } else if (v_tile >= 0 && lane == 0) {
+    // ---------------- V producer of one tile ----------------
+    const int t = v_tile;
+    const Work wk = decode_work(p, blockIdx.x * NT + t, BN);
+    volatile int never = 0;
+    if (wk.n_blk > 0) {
+      tma_prefetch_desc(&tm_v);
+      int issued = 0;
+      for (int j = 0; j < wk.n_blk; ++j) {
+        const int st = j % KSV;
+        if (j >= KSV && !mbar_wait(b_vempty(t, st), ((j / KSV) - 1) & 1, abort_flag)) break;
+        mbar_arrive_expect_tx(b_vfull(t, st), C::KV_BYTES);
+#pragma unroll
+        for (int a = 0; a < D / 64; ++a)
+          tma_load_3d(sV(t, st) + a * BN * 128, &tm_v, b_vfull(t, st), a * 64, wk.kvh, wk.kv_row(j, BN));
+        issued = j + 1;
+      }
+      for (int j = max(0, issued - KSV); j < issued; ++j)
+        mbar_wait(b_vfull(t, j % KSV), (j / KSV) & 1, &never, 1ll << 30);
     }
   } else if (warp == 1 && lane == 0) {
-    // ---------------- UMMA issuer ----------------
+    // ---------------- UMMA issuer, alternating between the tiles ----------------
     constexpr uint32_t idesc_s = umma_idesc_bf16(128, BN, 0, 0);
     constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 0, 1);
-    bool ok = mbar_wait(b_qfull, 0, abort_flag);
-    auto issue_s = [&](int j) -> bool {
-      const int st = j % KST;
-      if (!mbar_wait(b_kfull(st), (j / KST) & 1, abort_flag)) return false;
+    int nb[NT];
+    bool ok = true;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      nb[t] = decode_work(p, blockIdx.x * NT + t, BN).n_blk;
+      if (nb[t] > 0 && ok) ok = mbar_wait(b_qfull(t), 0, abort_flag);
+    }
+    auto issue_s = [&](int t, int j) -> bool {
+      const int st = j % KSK;
+      if (!mbar_wait(b_kfull(t, st), (j / KSK) & 1, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t d = tmem + ((j & 1) ? C::TM_S1 : C::TM_S0);
-      const uint32_t kb = sK + st * C::KV_BYTES;
+      const uint32_t d = tmem + t * C::TM_TILE + C::TM_S;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint64_t ad = umma_desc_sw128(sQ + (kk >> 2) * C::ATOM + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+        const uint64_t ad = umma_desc_sw128(sQ(t) + (kk >> 2) * C::ATOM + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = umma_desc_sw128(sK(t, st) + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
         umma_bf16_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
       }
-      umma_commit(b_sfull(j & 1));
-      umma_commit(b_kempty(st));
+      umma_commit(b_sfull(t));
+      umma_commit(b_kempty(t, st));
       return true;
     };
-    if (ok) ok = issue_s(0);
-    if (ok && n_blk > 1) ok = issue_s(1);
-    for (int j = 0; ok && j < n_blk; ++j) {
-      if (!mbar_wait(b_pfull, j & 1, abort_flag)) break;
-      const int st = j % KST;
-      if (!mbar_wait(b_vfull(st), (j / KST) & 1, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t vb = sV + st * C::KV_BYTES;
-      // P_j (bf16) sits in the first BN/2 columns of S_j's buffer.
-      const uint32_t pa = tmem + ((j & 1) ? C::TM_S1 : C::TM_S0);
 #pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk) {
-        const uint64_t bd = umma_desc_sw128(vb + kk * 16 * 128, BN * 128, 1024);
-        umma_bf16_ts(tmem + C::TM_O, pa + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+    for (int t = 0; t < NT; ++t)
+      if (ok && nb[t] > 0) ok = issue_s(t, 0);
+    int nmax = 0;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) nmax = max(nmax, nb[t]);
+    for (int j = 0; ok && j < nmax; ++j) {
+      // S_{j+1} as soon as the softmax has S_j in registers: it runs on the
+      // tensor cores while the softmax computes block j.  (s_free cannot
+      // lead this wait by two phases: the softmax only loads S_{j+1} after
+      // this issue.)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (!ok || j + 1 >= nb[t]) continue;
+        if (!mbar_wait(b_sfree(t), j & 1, abort_flag)) { ok = false; break; }
+        ok = issue_s(t, j + 1);
       }
-      umma_commit(b_odone);
-      umma_commit(b_vempty(st));
-      if (j + 2 < n_blk) ok = issue_s(j + 2);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (!ok || j >= nb[t]) continue;
+        // p_full[j&1] cannot lead by two phases: P_{j+2} is only written
+        // after PV_j (issued right below) completed.
+        if (!mbar_wait(b_pfull(t, j & 1), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+        const int st = j % KSV;
+        if (!mbar_wait(b_vfull(t, st), (j / KSV) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = tmem + t * C::TM_TILE + C::TM_P + (j & 1) * (BN / 2);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bd = umma_desc_sw128(sV(t, st) + kk * 16 * 128, BN * 128, 1024);
+          umma_bf16_ts(tmem + t * C::TM_TILE + C::TM_O, pa + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(b_odone(t, j & 1));
+        umma_commit(b_vempty(t, st));
+      }
     }
     // Every UMMA this thread issued has completed before TMEM is freed.
     umma_commit(b_drain);
     volatile int never = 0;
     mbar_wait(b_drain, 0, &never, 1ll << 30);
-  } else if (warp >= 4) {
-    // ---------------- softmax / correction / epilogue ----------------
+  } else if (warp >= 4 && warp < 4 + 4 * NT) {
+    // ---------------- softmax / correction / epilogue of one tile ----------------
+    const int t = (warp - 4) >> 2;
+    const Work wk = decode_work(p, blockIdx.x * NT + t, BN);
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
-    const int t = t0 + r / p.group;
+    const int tq = wk.t0 + r / p.group;
     const int h = r % p.group;
-    const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t tl = tmem + t * C::TM_TILE + ((uint32_t)(q4 * 32) << 16);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     float s[BN];
     uint32_t pk[BN / 2];
-    for (int j = 0; j < n_blk; ++j) {
-      if (!mbar_wait(b_sfull(j & 1), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+    for (int j = 0; j < wk.n_blk; ++j) {
+      // s_full cannot lead by two phases: S_{j+1} is only issued after this
+      // thread released S_j through s_free.
+      if (!mbar_wait(b_sfull(t), j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t sc = tl + ((j & 1) ? C::TM_S1 : C::TM_S0);
+      const uint32_t sc = tl + C::TM_S;
 #pragma unroll
       for (int c = 0; c < BN; c += 32) tmem_ld32(sc + c, s + c);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(b_sfree(t));
       // Key column c is visible if c <= lim: inside the prefix for a prefix
       // block, causal for an own block.  Full blocks skip the mask.
-      const int lim = (j < n_pre) ? seg.prefix_len - j * BN - 1 : t - (j - n_pre) * BN;
+      const int lim = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN - 1 : tq - (j - wk.n_pre) * BN;
       if (lim < BN - 1) {
 #pragma unroll
         for (int c = 0; c < BN; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
@@ -261,8 +341,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       const bool need = (j == 0) || (mb > m_run + 8.f);
       const float m_new = need ? mb : m_run;
       const float factor = (j > 0 && need) ? fast_exp2(m_run - m_new) : 1.f;
-      // P = 2^(s*scale - m): one FFMA + one ex2 per element, computed while
-      // the previous block's PV is still on the tensor cores.
+      // P = 2^(s*scale - m): one FFMA + one ex2 per element.
       const float neg = -m_new;
       float sm8[8];
 #pragma unroll
@@ -276,23 +355,28 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         pk[c >> 1] = pack_bf16x2(e0, e1);
       }
       const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
+      // P buffer j&1 is free once PV_{j-2} completed.  o_done[j&1] is not
+      // behind by a phase (PV_{j-4} was waited here two blocks ago) nor
+      // ahead (PV_j needs P_j).
+      if (j >= 2) {
+        if (!mbar_wait(b_odone(t, j & 1), ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+      }
       if (__any_sync(0xffffffffu, factor != 1.f)) {
         // O is rescaled in TMEM: PV of the previous block must be done (and
         // PV of this block cannot start before P_j is signalled).
-        if (!mbar_wait(b_odone, (j - 1) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(b_odone(t, (j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        {
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            float o[32];
-            tmem_ld32(tl + C::TM_O + c, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(tl + C::TM_O + c, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= factor;
-            tmem_st32(tl + C::TM_O + c, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] *= factor;
+          tmem_st32(tl + C::TM_O + c, o);
         }
+        tmem_wait_st();
       }
       l_run = l_run * factor + sum;
       m_run = m_new;
@@ -300,32 +384,36 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // rows are whatever the buffer holds there (possibly NaN/Inf, and
       // 0 * NaN = NaN in the MMA): zero them before PV reads the stage.
       {
-        const int vcount = (j < n_pre) ? seg.prefix_len - j * BN : (t0 + nt) - (j - n_pre) * BN;
+        const int vcount = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN : (wk.t0 + wk.nt) - (j - wk.n_pre) * BN;
         if (vcount < BN) {
-          const int vst = j % KST;
-          if (!mbar_wait(b_vfull(vst), (j / KST) & 1, abort_flag)) { ok = false; break; }
+          const int vst = j % KSV;
+          if (!mbar_wait(b_vfull(t, vst), (j / KSV) & 1, abort_flag)) { ok = false; break; }
           const int rows0 = vcount < 0 ? 0 : vcount;
           const int chunks = (BN - rows0) * 8 * (D / 64);
-          uint8_t* vb = smem + C::OFF_V + vst * C::KV_BYTES;
-          for (int i = threadIdx.x - 128; i < chunks; i += 128) {
+          uint8_t* vb = smem + t * C::T_BYTES + C::T_OFF_V + vst * C::KV_BYTES;
+          for (int i = q4 * 32 + lane; i < chunks; i += 128) {
             const int a = i / ((BN - rows0) * 8), rem = i % ((BN - rows0) * 8);
             *reinterpret_cast<uint4*>(vb + a * BN * 128 + (rows0 + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
           }
           fence_proxy_async_smem();
         }
       }
-      // P_j overwrites the (already read) S_j in TMEM, packed bf16x2.
+      // P_j into its TMEM buffer, packed bf16x2.
 #pragma unroll
-      for (int c = 0; c < BN / 2; c += 32) tmem_st32(sc + c, reinterpret_cast<const float*>(pk + c));
+      for (int c = 0; c < BN / 2; c += 32)
+        tmem_st32(tl + C::TM_P + (j & 1) * (BN / 2) + c, reinterpret_cast<const float*>(pk + c));
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(b_pfull);
+      mbar_arrive(b_pfull(t, j & 1));
     }
-    if (ok && mbar_wait(b_odone, (n_blk - 1) & 1, abort_flag)) {
+    // PV of the last block completed (its commit covers every earlier UMMA).
+    if (ok && wk.n_blk > 0 &&
+        mbar_wait(b_odone(t, (wk.n_blk - 1) & 1), ((wk.n_blk - 1) >> 1) & 1, abort_flag)) {
       tc_fence_after();
       const float inv = 1.f / l_run;
-      const bool store = (t < seg.q_len) && (r / p.group < nt);
-      __nv_bfloat16* orow = p.o + (size_t)(seg.q_start + t) * p.o_row_stride + (size_t)(kvh * p.group + h) * D;
+      const bool store = (tq < wk.seg.q_len) && (r / p.group < wk.nt);
+      __nv_bfloat16* orow =
+          p.o + (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D;
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         float o[32];
@@ -334,12 +422,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (store) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            uint4 pk;
-            pk.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
-            pk.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
-            pk.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
-            pk.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c + i) = pk;
+            uint4 pv;
+            pv.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
+            pv.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+            pv.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+            pv.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c + i) = pv;
           }
         }
       }
@@ -384,11 +472,11 @@ static int make_map(CUtensorMap* m, const void* base, int D, int heads, int rows
   return CEVK_OK;
 }
 
-template <int D, int BN, int KST>
+template <int D, int BN, int KSK, int KSV, int NT>
 static int launch_tc(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
                      int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
                      cudaStream_t stream) {
-  using C = AttnTc<D, BN, KST>;
+  using C = AttnTc<D, BN, KSK, KSV, NT>;
   const int group = hq / hkv, rows_t = 128 / group;
   CUtensorMap tq, tk, tv;
   int rc;
@@ -397,7 +485,7 @@ static int launch_tc(const void* q, const void* k, const void* v, void* o, int n
   if ((rc = make_map(&tv, v, D, hkv, n_kv_rows, kv_rs, 1, BN))) return rc;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<D, BN, KST>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+    if (cudaFuncSetAttribute(attn_tc_kernel<D, BN, KSK, KSV, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return set_error(CEVK_E_CUDA, "cannot opt in to %d B of shared memory", C::SMEM);
     attr = true;
@@ -406,13 +494,15 @@ static int launch_tc(const void* q, const void* k, const void* v, void* o, int n
   prm.o = reinterpret_cast<__nv_bfloat16*>(o);
   prm.segs = segs;
   prm.n_segs = n_segs;
+  prm.n_work = n_tiles * hkv;
   prm.hq = hq;
   prm.hkv = hkv;
   prm.group = group;
   prm.rows_t = rows_t;
   prm.o_row_stride = o_rs;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  attn_tc_kernel<D, BN, KST><<<(unsigned)n_tiles * hkv, 256, C::SMEM, stream>>>(tq, tk, tv, prm);
+  const unsigned grid = (unsigned)((prm.n_work + NT - 1) / NT);
+  attn_tc_kernel<D, BN, KSK, KSV, NT><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, prm);
   return check_launch("attn_tc_kernel");
 }
 
@@ -421,14 +511,14 @@ int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_t
                    cudaStream_t stream) {
   switch (D) {
     case 64:
-      return launch_tc<64, 64, 3>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                  scale, stream);
+      return launch_tc<64, 64, 6, 4, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
+                                     scale, stream);
     case 128:
-      return launch_tc<128, 64, 2>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                   scale, stream);
+      return launch_tc<128, 64, 3, 2, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
+                                      scale, stream);
     case 256:
-      return launch_tc<256, 64, 2>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                   scale, stream);
+      return launch_tc<256, 64, 3, 2, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
+                                      scale, stream);
     default:
       return set_error(CEVK_E_SHAPE, "bf16 attention supports head_dim 64, 128, 256 (got %d)", D);
   }

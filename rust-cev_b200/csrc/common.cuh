@@ -8,13 +8,20 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/cevk.h"
+#include "cevk.h"
 
 namespace cevk {
 
 // Error flag written by device code when a bounded wait gives up.  The host
 // reads it with cevk_device_status().
 extern __device__ int g_device_error;
+// Where the first bounded wait that gave up was: block, thread, barrier
+// shared-memory offset, parity.
+extern __device__ int g_device_error_info[4];
+// Up to 16 further waits that stopped because their CTA aborted:
+// {block, thread, barrier offset, parity} each; slot count in g_device_error_n.
+extern __device__ int g_device_error_n;
+extern __device__ int g_device_error_more[64];
 
 constexpr int kErrWaitTimeout = 1;
 
@@ -97,10 +104,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
-      if (*abort) return false;
+      if (*abort) {
+        const int k = atomicAdd(&g_device_error_n, 1);
+        if (k < 16) {
+          g_device_error_more[4 * k] = (int)blockIdx.x;
+          g_device_error_more[4 * k + 1] = (int)threadIdx.x;
+          g_device_error_more[4 * k + 2] = (int)bar;
+          g_device_error_more[4 * k + 3] = (int)parity;
+        }
+        return false;
+      }
       if (clock64() - t0 > limit) {
         *abort = 1;
-        atomicExch(&g_device_error, kErrWaitTimeout);
+        if (atomicExch(&g_device_error, kErrWaitTimeout) == 0) {
+          g_device_error_info[0] = (int)blockIdx.x;
+          g_device_error_info[1] = (int)threadIdx.x;
+          g_device_error_info[2] = (int)bar;
+          g_device_error_info[3] = (int)parity;
+        }
         return false;
       }
     }

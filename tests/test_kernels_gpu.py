@@ -18,20 +18,37 @@ def cuda():
     return torch.device("cuda")
 
 
-def oracle_segments(q, k, v, segs, scale=None):
+def oracle_segments(q, k, v, segs, scale=None, model_dtype=torch.float32):
     """Attention per segment with the reference's generic path
-    (qwen3.rs:206-220) on CPU f32: prefix rows in full, own rows causally."""
-    q, k, v = q.float().cpu(), k.float().cpu(), v.float().cpu()
-    out = torch.zeros_like(q)
+    (qwen3.rs:206-220) on CPU: prefix rows in full, own rows causally.
+    ``model_dtype`` is the dtype the reference computes q k^T and P V in
+    (P cast to it before P V); f32 gives the exact result."""
+    q, k, v = (x.cpu().to(model_dtype) for x in (q, k, v))
+    out = torch.zeros(q.shape)
     for (qs, ql, po, pl, so) in segs:
         if ql == 0:
             continue
         kk = torch.cat([k[po:po + pl], k[so:so + ql]], 0)
         vv = torch.cat([v[po:po + pl], v[so:so + ql]], 0)
-        mask = ref.causal_mask(ql, pl)
+        mask = ref.causal_mask(ql, pl).to(model_dtype)
         o = ref.attend(q[qs:qs + ql].transpose(0, 1)[None], kk.transpose(0, 1)[None], vv.transpose(0, 1)[None], mask)
-        out[qs:qs + ql] = o[0].transpose(0, 1)
+        out[qs:qs + ql] = o[0].transpose(0, 1).float()
     return out
+
+
+def check_bf16_attention(out, q, k, v, segs, n_tok):
+    """The kernel must be within 2e-2 of the exact result (the bound the
+    decision forward is held to) AND at least as accurate as the
+    reference's own bf16 arithmetic on the same inputs."""
+    exact = oracle_segments(q, k, v, segs)
+    ref_bf16 = oracle_segments(q, k, v, segs, model_dtype=torch.bfloat16)
+    rows = torch.zeros(n_tok, dtype=torch.bool)
+    for (qs, ql, *_r) in segs:
+        rows[qs:qs + ql] = True
+    err = (out.float().cpu()[rows] - exact[rows]).abs().max().item()
+    ref_err = (ref_bf16[rows] - exact[rows]).abs().max().item()
+    assert err < BF16_TOL, err
+    assert err <= ref_err + 1e-4, (err, ref_err)
 
 
 def rand_attn(n_tok, n_kv, hq, hkv, D, dtype, seed):
@@ -64,12 +81,7 @@ def test_attention_bf16_matches_oracle(case):
     plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda")
     out = ops.attend_packed(q, k, v, plan)
     ops.device_status()
-    want = oracle_segments(q, k, v, segs)
-    rows = torch.zeros(n_tok, dtype=torch.bool)
-    for (qs, ql, *_r) in segs:
-        rows[qs:qs + ql] = True
-    err = (out.float().cpu()[rows] - want[rows]).abs().max().item()
-    assert err < BF16_TOL, err
+    check_bf16_attention(out, q, k, v, segs, n_tok)
 
 
 @pytest.mark.parametrize("case", [0, 1, 3])
@@ -135,9 +147,7 @@ def test_attention_cfg2_shape_sampled():
     ops.device_status()
     for rq in (0, 17, 31):
         segs = [s for s in wb.segments if s[0] // 1024 == rq]
-        want = oracle_segments(wb.q, wb.k, wb.v, segs)
-        sl = slice(rq * 1024, (rq + 1) * 1024)
-        assert (out[sl].float().cpu() - want[sl]).abs().max().item() < BF16_TOL
+        check_bf16_attention(out, wb.q, wb.k, wb.v, segs, wb.n_tokens)
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-5)])
