@@ -11,6 +11,12 @@ do not count.  With --gpus N (torchrun, one rank per GPU) every rank runs its
 own batch (weak scaling, no collective on the data path); the time is the max
 over ranks.
 
+`--op gdn` / `--op conv` time one kernel alone at a config's layer shape
+(the Qwen3.5 gated-delta-rule chunked prefill of cfg4; the LFM2 gated
+short conv of cfg5) and print their own line with a roofline; `--op cfg3`,
+`cfg4`, `cfg5` run only that config's decisions/sec measurement.  These
+lines are for profiling and the per-kernel roofline, not the headline.
+
 `value` is kernel throughput with inputs resident in HBM; `e2e` is the same
 metric through the C ABI call with host buffers: pinned host -> device copies
 of Q, K, V and the segment table, the call, and the device -> host copy of O
@@ -257,6 +263,94 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
             "seconds": dt.item(), "workload": f"{name}: {plen}-token state, {nq} questions, rows continuing the state"}
 
 
+def timed(fn, steps, warmup, stream):
+    """Average device time (ms) of fn() over `steps` after `warmup` calls."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def gdn_flops(T: int, nv: int, dk: int, dv: int, chunk: int = 64) -> float:
+    """Algorithmic FLOPs of the chunked gated delta rule per call: per chunk
+    of C tokens and value head, K K^T and Q K^T (2 C^2 dk each), the WY
+    products W = T beta K and U = T beta V (2 C^2 dk, 2 C^2 dv), U - W S,
+    Q S and the state update K^T U' (2 C dk dv each) and the intra-chunk
+    (Q K^T * mask) U' (2 C^2 dv)."""
+    n_chunks = (T + chunk - 1) // chunk
+    C = chunk
+    per = 2 * C * C * (3 * dk + 2 * dv) + 6 * C * dk * dv
+    return float(n_chunks * nv * per)
+
+
+def op_bench(args, dev):
+    """One kernel alone at a config's layer shape (synthetic inputs)."""
+    import torch
+    from cev_b200 import ops
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device=dev).manual_seed(7)
+    peak_tf, peak_hbm, src = peaks()
+    if args.op == "gdn":
+        # cfg4 GDN layer, one 512-token prefill chunk continuing a state
+        B, T, nk, nv, dk, dv = 1, 512, 16, 32, 128, 128
+        C_ = 2 * nk * dk + nv * dv
+        conv_out = (torch.randn(B * T, C_, device=dev, generator=g) * 0.5).bfloat16()
+        ab = torch.randn(B * T, 2 * nv, device=dev, generator=g).bfloat16()
+        z = torch.randn(B * T, nv * dv, device=dev, generator=g).bfloat16()
+        a_log = torch.rand(nv, device=dev, generator=g) * 2
+        dt_bias = torch.rand(nv, device=dev, generator=g)
+        norm_w = (torch.rand(dv, device=dev, generator=g) + 0.5).bfloat16()
+        s_in = torch.randn(1, nv, dk, dv, device=dev, generator=g) * 0.1
+        s_out = torch.empty(B, nv, dk, dv, device=dev)
+        ws = torch.empty(ops.gdn_workspace_size(B, T, nv, dk, dv), dtype=torch.uint8, device=dev)
+        y = torch.empty(B * T, nv * dv, dtype=torch.bfloat16, device=dev)
+
+        def fn():
+            ops.gdn_chunk_prefill(conv_out, ab, 2 * nv, z, nv * dv, a_log, dt_bias, norm_w, 1e-6, s_in, s_out, B, T, nk,
+                                  nv, dk, dv, ws, out=y)
+        flops = gdn_flops(T, nv, dk, dv)
+        nbytes = (conv_out.numel() + ab.numel() + z.numel() + y.numel()) * 2 + (s_in.numel() + s_out.numel()) * 4
+        ms = timed(fn, args.steps, args.warmup, stream)
+        ops.device_status()
+        tf = flops / (ms / 1e3) / 1e12
+        line = {"metric": "gdn chunked prefill TFLOP/s (cfg4 layer, one 512-token chunk)", "value": tf,
+                "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
+                "config": {"workload": f"B{B} T{T} nk{nk} nv{nv} dk{dk} dv{dv}, chunk 64, state in/out",
+                           "flop_per_step": flops, "bytes_per_step": nbytes},
+                "roofline": {"bound": "compute (f32 SIMT)", "achieved": tf, "unit": "TFLOP/s",
+                             "hbm_gbs": nbytes / (ms / 1e3) / 1e9, "hbm_peak_gbs": peak_hbm, "peak_source": src}}
+    elif args.op == "conv":
+        # cfg5 gated short conv layer (d 2048, K 3) over a 16384-token run
+        B, T, d, K = 1, 16384, 2048, 3
+        bcx = torch.randn(B * T, 3 * d, device=dev, generator=g).bfloat16()
+        w = torch.randn(d, K, device=dev, generator=g).bfloat16()
+        tail_in = torch.randn(1, d, K - 1, device=dev, generator=g).bfloat16()
+        tail_out = torch.empty(B, d, K - 1, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(B * T, d, dtype=torch.bfloat16, device=dev)
+
+        def fn():
+            ops.short_conv(bcx, B, T, d, w, None, tail_in, tail_out, out=out)
+        nbytes = (bcx.numel() + out.numel()) * 2
+        ms = timed(fn, args.steps, args.warmup, stream)
+        ops.device_status()
+        gbs = nbytes / (ms / 1e3) / 1e9
+        line = {"metric": "gated short conv GB/s (cfg5 layer)", "value": gbs, "unit": "GB/s", "ms_per_step": ms,
+                "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
+                "config": {"workload": f"B{B} T{T} d{d} K{K} (inputs larger than L2)", "bytes_per_step": nbytes},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak_hbm, "unit": "GB/s",
+                             "frac": gbs / peak_hbm, "peak_source": src + " copy"}}
+    else:
+        raise SystemExit(f"unknown --op {args.op}")
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -268,6 +362,10 @@ def main():
                     help="also measure cfg3 decisions/sec on this many requests per GPU (0 = skip)")
     ap.add_argument("--hybrid", type=int, default=0,
                     help="also measure cfg4 and cfg5 decisions/sec on this many requests per GPU")
+    ap.add_argument("--op", default="attn", choices=["attn", "gdn", "conv", "cfg3", "cfg4", "cfg5"],
+                    help="attn: the headline line; gdn / conv: one kernel at its layer shape; "
+                         "cfg3/4/5: only that config's decisions/sec")
+    ap.add_argument("--requests", type=int, default=2, help="requests per GPU for --op cfg3/cfg4/cfg5")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -290,6 +388,20 @@ def main():
     def barrier():
         if world > 1:
             dist.barrier()
+
+    if args.op in ("gdn", "conv"):
+        if rank == 0:
+            op_bench(args, dev)
+    elif args.op in ("cfg3", "cfg4", "cfg5"):
+        res = (decisions_bench(args.requests, dev, world, dist) if args.op == "cfg3" else
+               hybrid_decisions_bench(args.op, args.requests, dev, world, dist))
+        if rank == 0:
+            print(json.dumps({"metric": f"{args.op} decisions/sec", **res}), flush=True)
+    if args.op != "attn":
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     wb = workloads.AttentionBatch(seed=1000 + rank, device=dev, **CFG)
     stream = torch.cuda.current_stream()

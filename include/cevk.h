@@ -83,8 +83,10 @@ int cevk_attn_schedule(cevk_segment* segs, int32_t n_segs, int32_t n_tokens, int
  * Query head h reads KV head h / (hq / hkv).  scale multiplies q.k
  * (the reference uses 1/sqrt(head_dim)).  segs_dev: device array of
  * n_segs descriptors as filled by cevk_attn_schedule.
- * bf16: head_dim 64, 128 or 256 on tcgen05 tensor cores; f32: any
- * head_dim <= 256 that is a multiple of 32. */
+ * bf16: head_dim 64, 128 or 256 on tcgen05 tensor cores, hq / hkv dividing
+ * 128, q/k/v/o 16-byte aligned and every row stride a multiple of 8
+ * (CEVK_E_SHAPE otherwise); f32: any head_dim <= 256 that is a multiple
+ * of 32. */
 int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
                              int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
                              int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,

@@ -49,28 +49,19 @@ int cevk_version(void) { return 100; }
 int cevk_device_status(void) {
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "device: %s", cudaGetErrorString(e));
-  int flag = 0, zero = 0;
-  if (cudaMemcpyFromSymbol(&flag, g_device_error, sizeof(int)) != cudaSuccess ||
-      cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess)
-    return set_error(CEVK_E_CUDA, "cannot read the device error flag");
-  if (flag) {
-    int info[4] = {0, 0, 0, 0}, zeros[4] = {0, 0, 0, 0};
-    cudaMemcpyFromSymbol(info, g_device_error_info, sizeof(info));
-    cudaMemcpyToSymbol(g_device_error_info, zeros, sizeof(zeros));
-    int n = 0, more[64];
-    cudaMemcpyFromSymbol(&n, g_device_error_n, sizeof(int));
-    cudaMemcpyFromSymbol(more, g_device_error_more, sizeof(more));
-    cudaMemcpyToSymbol(g_device_error_n, zeros, sizeof(int));
+  DeviceErrorRecord r;
+  if (!take_device_error(&r)) return set_error(CEVK_E_CUDA, "cannot read the device error flag");
+  if (r.flag) {
     char extra[384] = "";
     int len = 0;
-    for (int i = 0; i < n && i < 16 && len < 320; ++i)
-      if (more[4 * i] == info[0])
-        len += snprintf(extra + len, sizeof(extra) - len, " [t%d 0x%x p%d]", more[4 * i + 1], more[4 * i + 2],
-                        more[4 * i + 3]);
+    for (int i = 0; i < r.n && i < 16 && len < 320; ++i)
+      if (r.more[4 * i] == r.info[0])
+        len += snprintf(extra + len, sizeof(extra) - len, " [t%d 0x%x p%d]", r.more[4 * i + 1], r.more[4 * i + 2],
+                        r.more[4 * i + 3]);
     return set_error(CEVK_E_TIMEOUT,
                      "a bounded device wait gave up (code %d): block %d thread %d barrier smem offset 0x%x parity %d;"
                      " also stopped in that block:%s",
-                     flag, info[0], info[1], info[2], info[3], extra);
+                     r.flag, r.info[0], r.info[1], r.info[2], r.info[3], extra);
   }
   return CEVK_OK;
 }
@@ -114,9 +105,9 @@ int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* 
   if (n_segs == 0 || n_tiles == 0) return CEVK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == CEVK_BF16) {
-    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15)
-      return set_error(CEVK_E_SHAPE, "attention: q/k/v must be 16-byte aligned");
-    if ((q_row_stride % 8) || (kv_row_stride % 8))
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
+      return set_error(CEVK_E_SHAPE, "attention: q/k/v/o must be 16-byte aligned");
+    if ((q_row_stride % 8) || (kv_row_stride % 8) || (o_row_stride % 8))
       return set_error(CEVK_E_SHAPE, "attention: bf16 row strides must be multiples of 8 elements");
     if (128 % (hq / hkv) != 0) return set_error(CEVK_E_SHAPE, "attention: hq/hkv must divide 128");
     return attn_tc_launch(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,

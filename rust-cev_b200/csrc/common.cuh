@@ -13,15 +13,32 @@
 namespace cevk {
 
 // Error flag written by device code when a bounded wait gives up.  The host
-// reads it with cevk_device_status().
+// reads it with cevk_device_status().  Beside it: where the first bounded
+// wait that gave up was (block, thread, barrier shared-memory offset,
+// parity), and up to 16 further waits that stopped because their CTA aborted
+// ({block, thread, barrier offset, parity} each; slot count in
+// g_device_error_n).
 extern __device__ int g_device_error;
-// Where the first bounded wait that gave up was: block, thread, barrier
-// shared-memory offset, parity.
 extern __device__ int g_device_error_info[4];
-// Up to 16 further waits that stopped because their CTA aborted:
-// {block, thread, barrier offset, parity} each; slot count in g_device_error_n.
 extern __device__ int g_device_error_n;
 extern __device__ int g_device_error_more[64];
+
+// Reads and clears the error symbols (host side).
+struct DeviceErrorRecord {
+  int flag, info[4], n, more[64];
+};
+static inline bool take_device_error(DeviceErrorRecord* r) {
+  const int zeros[4] = {0, 0, 0, 0};
+  *r = DeviceErrorRecord{};
+  if (cudaMemcpyFromSymbol(&r->flag, g_device_error, sizeof(int)) != cudaSuccess) return false;
+  if (!r->flag) return true;
+  cudaMemcpyFromSymbol(r->info, g_device_error_info, sizeof(r->info));
+  cudaMemcpyFromSymbol(&r->n, g_device_error_n, sizeof(int));
+  cudaMemcpyFromSymbol(r->more, g_device_error_more, sizeof(r->more));
+  return cudaMemcpyToSymbol(g_device_error, zeros, sizeof(int)) == cudaSuccess &&
+         cudaMemcpyToSymbol(g_device_error_info, zeros, sizeof(zeros)) == cudaSuccess &&
+         cudaMemcpyToSymbol(g_device_error_n, zeros, sizeof(int)) == cudaSuccess;
+}
 
 constexpr int kErrWaitTimeout = 1;
 
@@ -97,9 +114,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // On timeout it raises the CTA abort flag and the device error flag and
 // returns false; callers then stop issuing work and fall through to the
 // kernel's clean-up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          long long limit = (1ll << 31)) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort, long long limit) {
   long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -126,6 +141,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       }
     }
   }
+}
+// The fast path (phase already complete) is one try_wait; the spin, clock
+// and diagnostics live out of line, which keeps a wait that does not block
+// at the try_wait round trip (~60 cycles; inlined, the same wait costs a UMMA
+// issuer ~160).
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                   long long limit) {
+  return mbar_wait_spin(bar, parity, abort, limit);
+}
+__device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity, volatile int* abort,
+                                               long long limit = (1ll << 31)) {
+  if (__builtin_expect(mbar_try_wait(bar, parity), 1)) return true;
+  return mbar_wait_slow(bar, parity, abort, limit);
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          long long limit = (1ll << 31)) {
+  return mbar_wait_fast(bar, parity, abort, limit);
 }
 
 // ----------------------------------------------------------------------------
