@@ -270,6 +270,12 @@ static size_t gdn_smem(int dk) {
   return sizeof(float) * (3 * GC * KP + 2 * GC * (GC + 1) + GC * GDVS + dk * GDVS + 3 * GC);
 }
 
+size_t gdn_tc_extra_floats(int B, int T, int nv, int dk, int dv);
+bool gdn_tc_supported(int dk, int dv);
+int gdn_tc_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
+               const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv, int dk,
+               int dv, cudaStream_t st);
+
 }  // namespace cevk
 
 using namespace cevk;
@@ -277,8 +283,9 @@ using namespace cevk;
 extern "C" {
 
 size_t cevk_gdn_workspace_size(int32_t B, int32_t T, int32_t nv, int32_t dk, int32_t dv) {
-  (void)dk;
-  return (size_t)B * T * nv * dv * sizeof(float);
+  // core output [B, T, nv, dv] f32, then (bf16 tensor-core path) the
+  // per-chunk W, q', k', U, intra and e^last of gdn_tc.cu.
+  return ((size_t)B * T * nv * dv + gdn_tc_extra_floats(B, T, nv, dk, dv)) * sizeof(float);
 }
 
 int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride, const void* z,
@@ -318,9 +325,16 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
   const long long rows = (long long)B * T;
   const unsigned ng = (unsigned)((rows * nv + 7) / 8);
   if (dtype == CEVK_BF16) {
-    cudaFuncSetAttribute(gdn_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gdn_chunk_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(prm);
-    int rc = check_launch("gdn_chunk_kernel");
+    int rc;
+    if (gdn_tc_supported(dk, dv) && ((uintptr_t)conv_out & 15) == 0 && C % 8 == 0) {
+      // tensor cores (gdn_tc.cu): chunk-parallel prep + state scan
+      rc = gdn_tc_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,
+                      nk, nv, dk, dv, st);
+    } else {
+      cudaFuncSetAttribute(gdn_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      gdn_chunk_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(prm);
+      rc = check_launch("gdn_chunk_kernel");
+    }
     if (rc) return rc;
     gdn_gated_norm_kernel<__nv_bfloat16><<<ng, 256, 0, st>>>(prm.core, (const __nv_bfloat16*)z, z_row_stride,
                                                              (const __nv_bfloat16*)norm_w, eps, (__nv_bfloat16*)y,

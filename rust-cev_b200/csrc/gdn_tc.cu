@@ -1,0 +1,533 @@
+// Gated DeltaNet chunked prefill on tensor cores (bf16 models): the same
+// chunked delta rule as gdn.cu (qwen35.rs:301-368), split into a
+// chunk-parallel phase and the sequential state scan, with every matrix
+// product on the tensor cores in split TF32 (mma.sync m16n8k8, f32
+// accumulate; x = hi + lo, three products hi*hi + hi*lo + lo*hi), which keeps
+// them at f32 accuracy: the reference runs the delta rule in f32.
+//
+// gdn_prep_kernel -- one CTA per (chunk of 64 tokens, value head, row):
+//   q, k <- l2norm (q * dk^-1/2); beta = sigmoid(b); g = -exp(A_log) *
+//   softplus(a + dt_bias); cum = cumsum(g) over the chunk;
+//   A = strict_lower(beta_i k_i.k_j e^(cum_i - cum_j)), T = (I + A)^-1 by
+//   forward substitution; intra = lower(q_i.k_j e^(cum_i - cum_j));
+//   W = T (k beta e^cum), U = T (v beta), q' = q e^cum, k' = k e^(last - cum).
+//   All of it to the workspace (f32).
+// gdn_scan_kernel -- one CTA per (value head, 32 value columns, row), over
+//   the chunks in order, state slice S (dk x 32) in shared memory:
+//   v_new = U - W S;  out = q' S + intra v_new;  S = e^last S + k'^T v_new.
+// The raw output goes to the workspace's core array; gdn.cu's gated-norm
+// kernel finishes y.
+#include "common.cuh"
+
+namespace cevk {
+
+namespace gtc {
+
+constexpr int C = 64;   // chunk length (qwen35.rs:302)
+constexpr int VS = 32;  // value columns per scan CTA
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// D += A(16x8, row) * B(8x8, col), TF32 in, f32 accumulate.
+__device__ __forceinline__ void mma_tf32(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// Fragments of m16n8k8 (lane = 4 * gid + tig):
+//   A: a0 (gid, tig), a1 (gid+8, tig), a2 (gid, tig+4), a3 (gid+8, tig+4)
+//   B: b0 (k = tig, n = gid), b1 (k = tig+4, n = gid)
+//   D: d0 (gid, 2tig), d1 (gid, 2tig+1), d2 (gid+8, 2tig), d3 (gid+8, 2tig+1)
+// SPLIT: x = hi + lo in TF32, D += hi*hi + hi*lo + lo*hi.
+template <bool SPLIT>
+struct Frag {
+  uint32_t hi[4], lo[4];
+  __device__ __forceinline__ void set(int i, float x) {
+    hi[i] = to_tf32(x);
+    if (SPLIT) lo[i] = to_tf32(x - __uint_as_float(hi[i]));
+  }
+};
+template <bool SPLIT>
+__device__ __forceinline__ void mma(float* d, const Frag<SPLIT>& a, const Frag<SPLIT>& b) {
+  mma_tf32(d, a.hi, b.hi);
+  if (SPLIT) {
+    mma_tf32(d, a.hi, b.lo);
+    mma_tf32(d, a.lo, b.hi);
+  }
+}
+// A fragment of a row-major matrix M (pitch ld) at (r0, k0), optionally with
+// a per-column scale.
+template <bool SPLIT>
+__device__ __forceinline__ Frag<SPLIT> frag_a(const float* M, int ld, int r0, int k0, int gid, int tig) {
+  Frag<SPLIT> f;
+  f.set(0, M[(r0 + gid) * ld + k0 + tig]);
+  f.set(1, M[(r0 + gid + 8) * ld + k0 + tig]);
+  f.set(2, M[(r0 + gid) * ld + k0 + tig + 4]);
+  f.set(3, M[(r0 + gid + 8) * ld + k0 + tig + 4]);
+  return f;
+}
+// A fragment of the transpose of row-major M: A(r, k) = M[k][r].
+template <bool SPLIT>
+__device__ __forceinline__ Frag<SPLIT> frag_at(const float* M, int ld, int r0, int k0, int gid, int tig) {
+  Frag<SPLIT> f;
+  f.set(0, M[(k0 + tig) * ld + r0 + gid]);
+  f.set(1, M[(k0 + tig) * ld + r0 + gid + 8]);
+  f.set(2, M[(k0 + tig + 4) * ld + r0 + gid]);
+  f.set(3, M[(k0 + tig + 4) * ld + r0 + gid + 8]);
+  return f;
+}
+// B fragment where B(k, n) = M[k][n] (row-major [K][N]); with row scale s[k].
+template <bool SPLIT>
+__device__ __forceinline__ Frag<SPLIT> frag_b(const float* M, int ld, int k0, int n0, int gid, int tig,
+                                              const float* s = nullptr) {
+  Frag<SPLIT> f;
+  const float x0 = M[(k0 + tig) * ld + n0 + gid], x1 = M[(k0 + tig + 4) * ld + n0 + gid];
+  f.set(0, s ? x0 * s[k0 + tig] : x0);
+  f.set(1, s ? x1 * s[k0 + tig + 4] : x1);
+  return f;
+}
+// B fragment where B(k, n) = M[n][k] (B = M^T, M row-major [N][K]).
+template <bool SPLIT>
+__device__ __forceinline__ Frag<SPLIT> frag_bt(const float* M, int ld, int k0, int n0, int gid, int tig) {
+  Frag<SPLIT> f;
+  f.set(0, M[(n0 + gid) * ld + k0 + tig]);
+  f.set(1, M[(n0 + gid) * ld + k0 + tig + 4]);
+  return f;
+}
+
+struct Params {
+  const __nv_bfloat16* conv;  // [B, T, Cc]: q (nk dk) | k (nk dk) | v (nv dv)
+  int Cc;
+  const __nv_bfloat16* ab;  // per token: b (nv) | a (nv)
+  int ab_rs;
+  const float* a_log;
+  const float* dt_bias;
+  const float* s_in;
+  long long s_bs;
+  float* s_out;
+  float* core;  // [B, T, nv, dv]
+  // per (row, chunk, head): W, q', k' [C][dk]; U [C][dv]; intra [C][C]; e^last
+  float *w, *qp, *kp, *u, *intra, *elast;
+  int B, T, nk, nv, dk, dv, n_chunks;
+};
+
+__host__ __device__ inline size_t chunk_index(const Params& p, int b, int ch, int h) {
+  return ((size_t)b * p.n_chunks + ch) * p.nv + h;
+}
+
+// ---------------------------------------------------------------------------
+template <int DK, int DV>
+__global__ void __launch_bounds__(128) gdn_prep_kernel(Params p) {
+  constexpr int KP = DK + 4, VP = DV + 4, AP = C + 4;
+  extern __shared__ float sm[];
+  float* sQ = sm;              // [C][KP]
+  float* sK = sQ + C * KP;     // [C][KP]
+  float* sV = sK + C * KP;     // [C][VP]
+  float* sA = sV + C * VP;     // [C][AP]
+  float* sT = sA + C * AP;     // [C][AP]
+  float* sG = sT + C * AP;     // cum [C]
+  float* sB = sG + C;          // beta [C]
+  float* sSw = sB + C;         // beta e^cum [C]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+  const int ch = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (p.nv / p.nk);  // key head shared by nv/nk value heads (qwen35.rs:436-441)
+  const int t0 = ch * C;
+  const int key_dim = p.nk * DK;
+
+  // ---- load q, k, v rows (bf16 -> f32), zero past T ----
+  for (int i = tid; i < C * (DK / 8); i += 128) {
+    const int r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
+    const int t = t0 + r;
+    uint4 qv = make_uint4(0, 0, 0, 0), kv = qv;
+    if (t < p.T) {
+      const __nv_bfloat16* row = p.conv + ((size_t)b * p.T + t) * p.Cc;
+      qv = *reinterpret_cast<const uint4*>(row + kh * DK + c8);
+      kv = *reinterpret_cast<const uint4*>(row + key_dim + kh * DK + c8);
+    }
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qv);
+    const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(&kv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      sQ[r * KP + c8 + e] = __bfloat162float(qb[e]);
+      sK[r * KP + c8 + e] = __bfloat162float(kb[e]);
+    }
+  }
+  for (int i = tid; i < C * (DV / 8); i += 128) {
+    const int r = i / (DV / 8), c8 = (i % (DV / 8)) * 8;
+    const int t = t0 + r;
+    uint4 vv = make_uint4(0, 0, 0, 0);
+    if (t < p.T) vv = *reinterpret_cast<const uint4*>(p.conv + ((size_t)b * p.T + t) * p.Cc + 2 * key_dim + h * DV + c8);
+    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&vv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sV[r * VP + c8 + e] = __bfloat162float(vb[e]);
+  }
+  if (tid < C) {
+    const int t = t0 + tid;
+    float beta = 0.f, g = 0.f;
+    if (t < p.T) {
+      const __nv_bfloat16* row = p.ab + ((size_t)b * p.T + t) * p.ab_rs;
+      beta = 1.f / (1.f + expf(-__bfloat162float(row[h])));
+      const float x = __bfloat162float(row[p.nv + h]) + p.dt_bias[h];
+      // softplus(x) = max(x, 0) + ln(1 + e^{-|x|}) (qwen35.rs:243-248)
+      g = (fmaxf(x, 0.f) + logf(1.f + expf(-fabsf(x)))) * -expf(p.a_log[h]);
+    }
+    sB[tid] = beta;
+    sG[tid] = g;
+  }
+  __syncthreads();
+  // ---- l2norm rows (warp per row), q * dk^-1/2; cumsum of g ----
+  const float qscale = rsqrtf((float)DK);
+  for (int r = warp; r < 2 * C; r += 4) {
+    float* row = r < C ? sQ + r * KP : sK + (r - C) * KP;
+    float ss = 0.f;
+    for (int d = lane; d < DK; d += 32) ss += row[d] * row[d];
+    ss = warp_sum(ss);
+    const float sc = (1.f / sqrtf(ss + 1e-6f)) * (r < C ? qscale : 1.f);
+    for (int d = lane; d < DK; d += 32) row[d] *= sc;
+  }
+  if (tid == 0) {
+    float acc = 0.f;
+    for (int r = 0; r < C; ++r) {
+      acc += sG[r];
+      sG[r] = acc;
+    }
+  }
+  __syncthreads();
+  if (tid < C) sSw[tid] = sB[tid] * expf(sG[tid]);
+
+  // ---- A = strict_lower(beta_i k_i.k_j dec), intra = lower(q_i.k_j dec) ----
+  {
+    const int r0 = warp * 16;
+    float ak[8][4], aq[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ak[n][e] = aq[n][e] = 0.f;
+#pragma unroll 1
+    for (int k0 = 0; k0 < DK; k0 += 8) {
+      const Frag<true> fk = frag_a<true>(sK, KP, r0, k0, gid, tig);
+      const Frag<true> fq = frag_a<true>(sQ, KP, r0, k0, gid, tig);
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        if (n * 8 > r0 + 15) continue;  // strictly above the diagonal block
+        const Frag<true> fb = frag_bt<true>(sK, KP, k0, n * 8, gid, tig);
+        mma<true>(ak[n], fk, fb);
+        mma<true>(aq[n], fq, fb);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = r0 + gid + (e >> 1) * 8, j = n * 8 + 2 * tig + (e & 1);
+        float a = 0.f, q = 0.f;
+        if (j <= i) {
+          const float dec = expf(sG[i] - sG[j]);
+          q = aq[n][e] * dec;
+          if (j < i) a = sB[i] * ak[n][e] * dec;
+        }
+        sA[i * AP + j] = a;
+        p.intra[chunk_index(p, b, ch, h) * C * C + i * C + j] = q;
+      }
+  }
+  __syncthreads();
+  // ---- T = (I + A)^-1 (threads 0-63, one column each) while threads 64-127
+  //      write q' = q e^cum and k' = k e^(last - cum) ----
+  const size_t ci = chunk_index(p, b, ch, h);
+  if (tid < C) {
+    const int c = tid;
+    for (int i = 0; i < C; ++i) {
+      float x = i == c ? 1.f : 0.f;
+      if (i > c) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int j = c;
+        for (; j + 3 < i; j += 4) {
+          a0 += sA[i * AP + j] * sT[j * AP + c];
+          a1 += sA[i * AP + j + 1] * sT[(j + 1) * AP + c];
+          a2 += sA[i * AP + j + 2] * sT[(j + 2) * AP + c];
+          a3 += sA[i * AP + j + 3] * sT[(j + 3) * AP + c];
+        }
+        for (; j < i; ++j) a0 += sA[i * AP + j] * sT[j * AP + c];
+        x = -((a0 + a1) + (a2 + a3));
+      }
+      sT[i * AP + c] = x;
+    }
+  } else {
+    const float last = sG[C - 1];
+    float* qp = p.qp + ci * C * DK;
+    float* kp = p.kp + ci * C * DK;
+    for (int i = tid - C; i < C * DK; i += 64) {
+      const int r = i / DK, d = i % DK;
+      qp[i] = sQ[r * KP + d] * expf(sG[r]);
+      kp[i] = sK[r * KP + d] * expf(last - sG[r]);
+    }
+    if (tid == C) p.elast[ci] = expf(last);
+  }
+  __syncthreads();
+  // ---- W = T (k beta e^cum), U = T (v beta) (T lower triangular) ----
+  {
+    const int r0 = warp * 16;
+    const int kend = r0 + 16;  // T[i][j] = 0 for j > i
+    float* wo = p.w + ci * C * DK;
+    float* uo = p.u + ci * C * DV;
+#pragma unroll 1
+    for (int half = 0; half < DK / 64; ++half) {  // 64 output columns at a time
+      float acc[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+#pragma unroll 1
+      for (int k0 = 0; k0 < kend; k0 += 8) {
+        const Frag<true> fa = frag_a<true>(sT, AP, r0, k0, gid, tig);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const Frag<true> fb = frag_b<true>(sK, KP, k0, half * 64 + n * 8, gid, tig, sSw);
+          mma<true>(acc[n], fa, fb);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int col = half * 64 + n * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(wo + (r0 + gid) * DK + col) = make_float2(acc[n][0], acc[n][1]);
+        *reinterpret_cast<float2*>(wo + (r0 + gid + 8) * DK + col) = make_float2(acc[n][2], acc[n][3]);
+      }
+    }
+#pragma unroll 1
+    for (int half = 0; half < DV / 64; ++half) {
+      float acc[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+#pragma unroll 1
+      for (int k0 = 0; k0 < kend; k0 += 8) {
+        const Frag<true> fa = frag_a<true>(sT, AP, r0, k0, gid, tig);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const Frag<true> fb = frag_b<true>(sV, VP, k0, half * 64 + n * 8, gid, tig, sB);
+          mma<true>(acc[n], fa, fb);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int col = half * 64 + n * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(uo + (r0 + gid) * DV + col) = make_float2(acc[n][0], acc[n][1]);
+        *reinterpret_cast<float2*>(uo + (r0 + gid + 8) * DV + col) = make_float2(acc[n][2], acc[n][3]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int DK, int DV>
+__global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
+  constexpr int KP = DK + 4, SP = VS + 8, AP = C + 4;
+  extern __shared__ float sm[];
+  float* sS = sm;               // [DK][SP]   state slice
+  float* sW = sS + DK * SP;     // [C][KP]
+  float* sQp = sW + C * KP;     // [C][KP]
+  float* sKp = sQp + C * KP;    // [C][KP]
+  float* sU = sKp + C * KP;     // [C][SP]    U slice, then v_new
+  float* sI = sU + C * SP;      // [C][AP]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+  const int sl = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int c0 = sl * VS;
+
+  for (int i = tid; i < DK * VS; i += 128) {
+    const int d = i / VS, c = i % VS;
+    sS[d * SP + c] = p.s_in ? p.s_in[b * p.s_bs + ((size_t)h * DK + d) * DV + c0 + c] : 0.f;
+  }
+  for (int ch = 0; ch < p.n_chunks; ++ch) {
+    const size_t ci = chunk_index(p, b, ch, h);
+    __syncthreads();  // previous chunk done with sW .. sI; state slice written
+    {
+      const float4* w4 = reinterpret_cast<const float4*>(p.w + ci * C * DK);
+      const float4* q4 = reinterpret_cast<const float4*>(p.qp + ci * C * DK);
+      const float4* k4 = reinterpret_cast<const float4*>(p.kp + ci * C * DK);
+      for (int i = tid; i < C * DK / 4; i += 128) {
+        const int r = (i * 4) / DK, d = (i * 4) % DK;
+        *reinterpret_cast<float4*>(sW + r * KP + d) = w4[i];
+        *reinterpret_cast<float4*>(sQp + r * KP + d) = q4[i];
+        *reinterpret_cast<float4*>(sKp + r * KP + d) = k4[i];
+      }
+      const float* u = p.u + ci * C * DV + c0;
+      for (int i = tid; i < C * VS / 4; i += 128) {
+        const int r = (i * 4) / VS, c = (i * 4) % VS;
+        *reinterpret_cast<float4*>(sU + r * SP + c) = *reinterpret_cast<const float4*>(u + r * DV + c);
+      }
+      const float4* in4 = reinterpret_cast<const float4*>(p.intra + ci * C * C);
+      for (int i = tid; i < C * C / 4; i += 128) {
+        const int r = (i * 4) / C, c = (i * 4) % C;
+        *reinterpret_cast<float4*>(sI + r * AP + c) = in4[i];
+      }
+    }
+    const float el = p.elast[ci];
+    __syncthreads();
+    const int r0 = warp * 16;
+    float vn[4][4], o[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) vn[n][e] = o[n][e] = 0.f;
+    // W S and q' S over dk
+#pragma unroll 1
+    for (int k0 = 0; k0 < DK; k0 += 8) {
+      const Frag<true> fw = frag_a<true>(sW, KP, r0, k0, gid, tig);
+      const Frag<true> fq = frag_a<true>(sQp, KP, r0, k0, gid, tig);
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const Frag<true> fs = frag_b<true>(sS, SP, k0, n * 8, gid, tig);
+        mma<true>(vn[n], fw, fs);
+        mma<true>(o[n], fq, fs);
+      }
+    }
+    // v_new = U - W S (in place over U: each warp owns its 16 rows)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = r0 + gid + (e >> 1) * 8, j = n * 8 + 2 * tig + (e & 1);
+        sU[i * SP + j] -= vn[n][e];
+      }
+    __syncthreads();
+    // out = q' S + intra v_new (intra lower triangular)
+#pragma unroll 1
+    for (int k0 = 0; k0 < r0 + 16; k0 += 8) {
+      const Frag<true> fi = frag_a<true>(sI, AP, r0, k0, gid, tig);
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const Frag<true> fv = frag_b<true>(sU, SP, k0, n * 8, gid, tig);
+        mma<true>(o[n], fi, fv);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        const int t = ch * C + r0 + gid + hlf * 8;
+        if (t < p.T)
+          *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n * 8 + 2 * tig) =
+              make_float2(o[n][2 * hlf], o[n][2 * hlf + 1]);
+      }
+    // S = e^last S + k'^T v_new: warp w owns state rows 32w .. 32w+31
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int d0 = warp * 32 + m * 16;
+      float acc[4][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
+          acc[n][e] = sS[d * SP + c] * el;
+        }
+#pragma unroll 1
+      for (int k0 = 0; k0 < C; k0 += 8) {
+        const Frag<true> fk = frag_at<true>(sKp, KP, d0, k0, gid, tig);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const Frag<true> fv = frag_b<true>(sU, SP, k0, n * 8, gid, tig);
+          mma<true>(acc[n], fk, fv);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
+          sS[d * SP + c] = acc[n][e];
+        }
+    }
+  }
+  __syncthreads();
+  if (p.s_out)
+    for (int i = tid; i < DK * VS; i += 128) {
+      const int d = i / VS, c = i % VS;
+      p.s_out[(size_t)b * p.nv * DK * DV + ((size_t)h * DK + d) * DV + c0 + c] = sS[d * SP + c];
+    }
+}
+
+template <int DK, int DV>
+size_t prep_smem() {
+  return sizeof(float) * (2 * C * (DK + 4) + C * (DV + 4) + 2 * C * (C + 4) + 3 * C);
+}
+template <int DK, int DV>
+size_t scan_smem() {
+  return sizeof(float) * (DK * (VS + 8) + 3 * C * (DK + 4) + C * (VS + 8) + C * (C + 4));
+}
+
+template <int DK, int DV>
+int launch(const Params& p, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gdn_prep_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)prep_smem<DK, DV>()) != cudaSuccess ||
+        cudaFuncSetAttribute(gdn_scan_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)scan_smem<DK, DV>()) != cudaSuccess)
+      return set_error(CEVK_E_CUDA, "gdn: cannot opt in to the shared memory of the tensor-core kernels");
+    attr = true;
+  }
+  gdn_prep_kernel<DK, DV><<<dim3(p.n_chunks, p.nv, p.B), 128, prep_smem<DK, DV>(), st>>>(p);
+  int rc = check_launch("gdn_prep_kernel");
+  if (rc) return rc;
+  gdn_scan_kernel<DK, DV><<<dim3(DV / VS, p.nv, p.B), 128, scan_smem<DK, DV>(), st>>>(p);
+  return check_launch("gdn_scan_kernel");
+}
+
+}  // namespace gtc
+
+// Workspace floats of the tensor-core path beyond the core output.
+size_t gdn_tc_extra_floats(int B, int T, int nv, int dk, int dv) {
+  const size_t nc = (size_t)(T + gtc::C - 1) / gtc::C;
+  return (size_t)B * nc * nv * ((size_t)gtc::C * (3 * dk + dv + gtc::C) + 1);
+}
+
+bool gdn_tc_supported(int dk, int dv) { return (dk == 128 && dv == 128) || (dk == 64 && dv == 64); }
+
+int gdn_tc_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
+               const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv, int dk,
+               int dv, cudaStream_t st) {
+  gtc::Params p;
+  p.conv = reinterpret_cast<const __nv_bfloat16*>(conv_out);
+  p.Cc = C_;
+  p.ab = reinterpret_cast<const __nv_bfloat16*>(ab);
+  p.ab_rs = ab_rs;
+  p.a_log = a_log;
+  p.dt_bias = dt_bias;
+  p.s_in = s_in;
+  p.s_bs = s_bs;
+  p.s_out = s_out;
+  p.B = B;
+  p.T = T;
+  p.nk = nk;
+  p.nv = nv;
+  p.dk = dk;
+  p.dv = dv;
+  p.n_chunks = (T + gtc::C - 1) / gtc::C;
+  const size_t per = (size_t)B * p.n_chunks * nv * gtc::C;
+  p.core = workspace;
+  float* x = workspace + (size_t)B * T * nv * dv;
+  p.w = x;
+  x += per * dk;
+  p.qp = x;
+  x += per * dk;
+  p.kp = x;
+  x += per * dk;
+  p.u = x;
+  x += per * dv;
+  p.intra = x;
+  x += per * gtc::C;
+  p.elast = x;
+  if (dk == 128) return gtc::launch<128, 128>(p, st);
+  return gtc::launch<64, 64>(p, st);
+}
+
+}  // namespace cevk
