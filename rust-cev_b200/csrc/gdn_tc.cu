@@ -3,7 +3,10 @@
 // chunk-parallel phase and the sequential state scan, with every matrix
 // product on the tensor cores in split TF32 (mma.sync m16n8k8, f32
 // accumulate; x = hi + lo, three products hi*hi + hi*lo + lo*hi), which keeps
-// them at f32 accuracy: the reference runs the delta rule in f32.
+// them at f32 accuracy: the reference runs the delta rule in f32, the state
+// carries every chunk's error forward, and a bf16 model amplifies small
+// output differences layer by layer (plain TF32 on the output-only products
+// measured at the edge of the model-level bound).
 //
 // gdn_prep_kernel -- one CTA per (chunk of 64 tokens, value head, row):
 //   q, k <- l2norm (q * dk^-1/2); beta = sigmoid(b); g = -exp(A_log) *
@@ -102,6 +105,13 @@ __device__ __forceinline__ Frag<SPLIT> frag_bt(const float* M, int ld, int k0, i
   return f;
 }
 
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 struct Params {
   const __nv_bfloat16* conv;  // [B, T, Cc]: q (nk dk) | k (nk dk) | v (nv dv)
   int Cc;
@@ -123,50 +133,42 @@ __host__ __device__ inline size_t chunk_index(const Params& p, int b, int ch, in
 }
 
 // ---------------------------------------------------------------------------
+// 103.7 KB of shared memory (dk = dv = 128): two CTAs per SM.  v reuses the
+// q buffer once q' is written.
 template <int DK, int DV>
-__global__ void __launch_bounds__(128) gdn_prep_kernel(Params p) {
-  constexpr int KP = DK + 4, VP = DV + 4, AP = C + 4;
+__global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
+  static_assert(DK == DV, "v is staged in the q buffer");
+  constexpr int KP = DK + 4, AP = C + 4;
+  constexpr int NL = C * (DK / 8) / 128;  // 16-byte loads per thread per matrix
   extern __shared__ float sm[];
-  float* sQ = sm;              // [C][KP]
-  float* sK = sQ + C * KP;     // [C][KP]
-  float* sV = sK + C * KP;     // [C][VP]
-  float* sA = sV + C * VP;     // [C][AP]
-  float* sT = sA + C * AP;     // [C][AP]
-  float* sG = sT + C * AP;     // cum [C]
-  float* sB = sG + C;          // beta [C]
-  float* sSw = sB + C;         // beta e^cum [C]
+  float* sQ = sm;             // [C][KP]  q, then v
+  float* sK = sQ + C * KP;    // [C][KP]
+  float* sA = sK + C * KP;    // [C][AP]  A (strict lower)
+  float* sT = sA + C * AP;    // [C][AP]  T = (I + A)^-1
+  float* sG = sT + C * AP;    // cum
+  float* sB = sG + C;         // beta
+  float* sSw = sB + C;        // beta e^cum
+  float* sEq = sSw + C;       // e^cum
+  float* sEk = sEq + C;       // e^(last - cum)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int ch = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.nv / p.nk);  // key head shared by nv/nk value heads (qwen35.rs:436-441)
   const int t0 = ch * C;
   const int key_dim = p.nk * DK;
+  const size_t ci = chunk_index(p, b, ch, h);
 
-  // ---- load q, k, v rows (bf16 -> f32), zero past T ----
-  for (int i = tid; i < C * (DK / 8); i += 128) {
-    const int r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
-    const int t = t0 + r;
-    uint4 qv = make_uint4(0, 0, 0, 0), kv = qv;
-    if (t < p.T) {
-      const __nv_bfloat16* row = p.conv + ((size_t)b * p.T + t) * p.Cc;
-      qv = *reinterpret_cast<const uint4*>(row + kh * DK + c8);
-      kv = *reinterpret_cast<const uint4*>(row + key_dim + kh * DK + c8);
-    }
-    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qv);
-    const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(&kv);
+  // ---- all q, k, v loads in flight at once (bf16), zero past T ----
+  uint4 qv[NL], kv[NL], vv[NL];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      sQ[r * KP + c8 + e] = __bfloat162float(qb[e]);
-      sK[r * KP + c8 + e] = __bfloat162float(kb[e]);
+  for (int u = 0; u < NL; ++u) {
+    const int i = tid + u * 128, r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
+    qv[u] = kv[u] = vv[u] = make_uint4(0, 0, 0, 0);
+    if (t0 + r < p.T) {
+      const __nv_bfloat16* row = p.conv + ((size_t)b * p.T + t0 + r) * p.Cc;
+      qv[u] = *reinterpret_cast<const uint4*>(row + kh * DK + c8);
+      kv[u] = *reinterpret_cast<const uint4*>(row + key_dim + kh * DK + c8);
+      vv[u] = *reinterpret_cast<const uint4*>(row + 2 * key_dim + h * DV + c8);
     }
-  }
-  for (int i = tid; i < C * (DV / 8); i += 128) {
-    const int r = i / (DV / 8), c8 = (i % (DV / 8)) * 8;
-    const int t = t0 + r;
-    uint4 vv = make_uint4(0, 0, 0, 0);
-    if (t < p.T) vv = *reinterpret_cast<const uint4*>(p.conv + ((size_t)b * p.T + t) * p.Cc + 2 * key_dim + h * DV + c8);
-    const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&vv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sV[r * VP + c8 + e] = __bfloat162float(vb[e]);
   }
   if (tid < C) {
     const int t = t0 + tid;
@@ -180,6 +182,17 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(Params p) {
     }
     sB[tid] = beta;
     sG[tid] = g;
+  }
+  auto unpack = [](const uint4& u, float* dst) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int x = 0; x < 8; ++x) dst[x] = __bfloat162float(e[x]);
+  };
+#pragma unroll
+  for (int u = 0; u < NL; ++u) {
+    const int i = tid + u * 128, r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
+    unpack(qv[u], sQ + r * KP + c8);
+    unpack(kv[u], sK + r * KP + c8);
   }
   __syncthreads();
   // ---- l2norm rows (warp per row), q * dk^-1/2; cumsum of g ----
@@ -200,7 +213,13 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(Params p) {
     }
   }
   __syncthreads();
-  if (tid < C) sSw[tid] = sB[tid] * expf(sG[tid]);
+  if (tid < C) {
+    const float last = sG[C - 1];
+    sSw[tid] = sB[tid] * expf(sG[tid]);
+    sEq[tid] = expf(sG[tid]);
+    sEk[tid] = expf(last - sG[tid]);
+    if (tid == 0) p.elast[ci] = expf(last);
+  }
 
   // ---- A = strict_lower(beta_i k_i.k_j dec), intra = lower(q_i.k_j dec) ----
   {
@@ -222,63 +241,78 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(Params p) {
         mma<true>(aq[n], fq, fb);
       }
     }
+    float* intra = p.intra + ci * C * C;
 #pragma unroll
     for (int n = 0; n < 8; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = r0 + gid + (e >> 1) * 8, j = n * 8 + 2 * tig + (e & 1);
-        float a = 0.f, q = 0.f;
-        if (j <= i) {
-          const float dec = expf(sG[i] - sG[j]);
-          q = aq[n][e] * dec;
-          if (j < i) a = sB[i] * ak[n][e] * dec;
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        const int i = r0 + gid + hlf * 8, j = n * 8 + 2 * tig;
+        float a[2], q[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          a[e] = q[e] = 0.f;
+          if (j + e <= i) {
+            const float dec = expf(sG[i] - sG[j + e]);
+            q[e] = aq[n][2 * hlf + e] * dec;
+            if (j + e < i) a[e] = sB[i] * ak[n][2 * hlf + e] * dec;
+          }
+          sA[i * AP + j + e] = a[e];
         }
-        sA[i * AP + j] = a;
-        p.intra[chunk_index(p, b, ch, h) * C * C + i * C + j] = q;
+        *reinterpret_cast<float2*>(intra + i * C + j) = make_float2(q[0], q[1]);
       }
   }
   __syncthreads();
-  // ---- T = (I + A)^-1 (threads 0-63, one column each) while threads 64-127
-  //      write q' = q e^cum and k' = k e^(last - cum) ----
-  const size_t ci = chunk_index(p, b, ch, h);
-  if (tid < C) {
-    const int c = tid;
+  // ---- T = (I + A)^-1, column c by forward substitution on a thread pair
+  //      (the two halves of each dot product, combined by a shuffle) ----
+  {
+    const int c = tid >> 1, half = tid & 1;
     for (int i = 0; i < C; ++i) {
-      float x = i == c ? 1.f : 0.f;
+      float a0 = 0.f, a1 = 0.f;
       if (i > c) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-        int j = c;
-        for (; j + 3 < i; j += 4) {
+        int j = c + half;
+        for (; j + 2 < i; j += 4) {
           a0 += sA[i * AP + j] * sT[j * AP + c];
-          a1 += sA[i * AP + j + 1] * sT[(j + 1) * AP + c];
-          a2 += sA[i * AP + j + 2] * sT[(j + 2) * AP + c];
-          a3 += sA[i * AP + j + 3] * sT[(j + 3) * AP + c];
+          a1 += sA[i * AP + j + 2] * sT[(j + 2) * AP + c];
         }
-        for (; j < i; ++j) a0 += sA[i * AP + j] * sT[j * AP + c];
-        x = -((a0 + a1) + (a2 + a3));
+        for (; j < i; j += 2) a0 += sA[i * AP + j] * sT[j * AP + c];
       }
-      sT[i * AP + c] = x;
+      float tot = a0 + a1;
+      tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+      if (half == 0) sT[i * AP + c] = i == c ? 1.f : (i > c ? -tot : 0.f);
+      __syncwarp();
     }
-  } else {
-    const float last = sG[C - 1];
+  }
+  // q' = q e^cum, k' = k e^(last - cum)
+  {
     float* qp = p.qp + ci * C * DK;
     float* kp = p.kp + ci * C * DK;
-    for (int i = tid - C; i < C * DK; i += 64) {
-      const int r = i / DK, d = i % DK;
-      qp[i] = sQ[r * KP + d] * expf(sG[r]);
-      kp[i] = sK[r * KP + d] * expf(last - sG[r]);
+    for (int i = tid; i < C * DK / 4; i += 128) {
+      const int r = (i * 4) / DK, d = (i * 4) % DK;
+      const float4 q4 = *reinterpret_cast<const float4*>(sQ + r * KP + d);
+      const float4 k4 = *reinterpret_cast<const float4*>(sK + r * KP + d);
+      const float eq = sEq[r], ek = sEk[r];
+      reinterpret_cast<float4*>(qp)[i] = make_float4(q4.x * eq, q4.y * eq, q4.z * eq, q4.w * eq);
+      reinterpret_cast<float4*>(kp)[i] = make_float4(k4.x * ek, k4.y * ek, k4.z * ek, k4.w * ek);
     }
-    if (tid == C) p.elast[ci] = expf(last);
+  }
+  __syncthreads();  // T complete; q no longer needed
+#pragma unroll
+  for (int u = 0; u < NL; ++u) {
+    const int i = tid + u * 128, r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
+    unpack(vv[u], sQ + r * KP + c8);
   }
   __syncthreads();
   // ---- W = T (k beta e^cum), U = T (v beta) (T lower triangular) ----
   {
     const int r0 = warp * 16;
     const int kend = r0 + 16;  // T[i][j] = 0 for j > i
-    float* wo = p.w + ci * C * DK;
-    float* uo = p.u + ci * C * DV;
 #pragma unroll 1
-    for (int half = 0; half < DK / 64; ++half) {  // 64 output columns at a time
+    for (int part = 0; part < 2 * (DK / 64); ++part) {  // 64 output columns of W, then of U
+      const bool is_u = part >= DK / 64;
+      const int cb = (part % (DK / 64)) * 64;
+      const float* src = is_u ? sQ : sK;
+      const float* scale = is_u ? sB : sSw;
+      float* dst = (is_u ? p.u : p.w) + ci * C * DK;
       float acc[8][4];
 #pragma unroll
       for (int n = 0; n < 8; ++n)
@@ -289,38 +323,15 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(Params p) {
         const Frag<true> fa = frag_a<true>(sT, AP, r0, k0, gid, tig);
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-          const Frag<true> fb = frag_b<true>(sK, KP, k0, half * 64 + n * 8, gid, tig, sSw);
+          const Frag<true> fb = frag_b<true>(src, KP, k0, cb + n * 8, gid, tig, scale);
           mma<true>(acc[n], fa, fb);
         }
       }
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
-        const int col = half * 64 + n * 8 + 2 * tig;
-        *reinterpret_cast<float2*>(wo + (r0 + gid) * DK + col) = make_float2(acc[n][0], acc[n][1]);
-        *reinterpret_cast<float2*>(wo + (r0 + gid + 8) * DK + col) = make_float2(acc[n][2], acc[n][3]);
-      }
-    }
-#pragma unroll 1
-    for (int half = 0; half < DV / 64; ++half) {
-      float acc[8][4];
-#pragma unroll
-      for (int n = 0; n < 8; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-#pragma unroll 1
-      for (int k0 = 0; k0 < kend; k0 += 8) {
-        const Frag<true> fa = frag_a<true>(sT, AP, r0, k0, gid, tig);
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const Frag<true> fb = frag_b<true>(sV, VP, k0, half * 64 + n * 8, gid, tig, sB);
-          mma<true>(acc[n], fa, fb);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const int col = half * 64 + n * 8 + 2 * tig;
-        *reinterpret_cast<float2*>(uo + (r0 + gid) * DV + col) = make_float2(acc[n][0], acc[n][1]);
-        *reinterpret_cast<float2*>(uo + (r0 + gid + 8) * DV + col) = make_float2(acc[n][2], acc[n][3]);
+        const int col = cb + n * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(dst + (r0 + gid) * DK + col) = make_float2(acc[n][0], acc[n][1]);
+        *reinterpret_cast<float2*>(dst + (r0 + gid + 8) * DK + col) = make_float2(acc[n][2], acc[n][3]);
       }
     }
   }
@@ -349,25 +360,27 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
     const size_t ci = chunk_index(p, b, ch, h);
     __syncthreads();  // previous chunk done with sW .. sI; state slice written
     {
-      const float4* w4 = reinterpret_cast<const float4*>(p.w + ci * C * DK);
-      const float4* q4 = reinterpret_cast<const float4*>(p.qp + ci * C * DK);
-      const float4* k4 = reinterpret_cast<const float4*>(p.kp + ci * C * DK);
+      // every 16-byte copy of the chunk in flight at once
+      const float* w = p.w + ci * C * DK;
+      const float* q = p.qp + ci * C * DK;
+      const float* k = p.kp + ci * C * DK;
       for (int i = tid; i < C * DK / 4; i += 128) {
         const int r = (i * 4) / DK, d = (i * 4) % DK;
-        *reinterpret_cast<float4*>(sW + r * KP + d) = w4[i];
-        *reinterpret_cast<float4*>(sQp + r * KP + d) = q4[i];
-        *reinterpret_cast<float4*>(sKp + r * KP + d) = k4[i];
+        cp_async16(sW + r * KP + d, w + 4 * i);
+        cp_async16(sQp + r * KP + d, q + 4 * i);
+        cp_async16(sKp + r * KP + d, k + 4 * i);
       }
       const float* u = p.u + ci * C * DV + c0;
       for (int i = tid; i < C * VS / 4; i += 128) {
         const int r = (i * 4) / VS, c = (i * 4) % VS;
-        *reinterpret_cast<float4*>(sU + r * SP + c) = *reinterpret_cast<const float4*>(u + r * DV + c);
+        cp_async16(sU + r * SP + c, u + r * DV + c);
       }
-      const float4* in4 = reinterpret_cast<const float4*>(p.intra + ci * C * C);
+      const float* in = p.intra + ci * C * C;
       for (int i = tid; i < C * C / 4; i += 128) {
         const int r = (i * 4) / C, c = (i * 4) % C;
-        *reinterpret_cast<float4*>(sI + r * AP + c) = in4[i];
+        cp_async16(sI + r * AP + c, in + 4 * i);
       }
+      cp_async_wait_all();
     }
     const float el = p.elast[ci];
     __syncthreads();
@@ -457,7 +470,7 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
 
 template <int DK, int DV>
 size_t prep_smem() {
-  return sizeof(float) * (2 * C * (DK + 4) + C * (DV + 4) + 2 * C * (C + 4) + 3 * C);
+  return sizeof(float) * (2 * C * (DK + 4) + 2 * C * (C + 4) + 5 * C);
 }
 template <int DK, int DV>
 size_t scan_smem() {
