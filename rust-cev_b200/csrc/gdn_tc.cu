@@ -183,10 +183,12 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
     sB[tid] = beta;
     sG[tid] = g;
   }
-  auto unpack = [](const uint4& u, float* dst) {
+  auto unpack = [](const uint4& u, float* dst) {  // 8 bf16 -> two 16-byte stores
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-    for (int x = 0; x < 8; ++x) dst[x] = __bfloat162float(e[x]);
+    reinterpret_cast<float4*>(dst)[0] =
+        make_float4(__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3]));
+    reinterpret_cast<float4*>(dst)[1] =
+        make_float4(__bfloat162float(e[4]), __bfloat162float(e[5]), __bfloat162float(e[6]), __bfloat162float(e[7]));
   };
 #pragma unroll
   for (int u = 0; u < NL; ++u) {
@@ -338,9 +340,14 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 }
 
 // ---------------------------------------------------------------------------
+// 8 warps: warp w computes rows 16 (w & 3) .. +16 of v_new / out for value
+// columns 16 (w >> 2) .. +16 of the slice, and state rows 16 w .. +16 in the
+// update (warps 0 .. dk/16 - 1).
+constexpr int SCAN_THREADS = 256;
 template <int DK, int DV>
-__global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
+__global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
   constexpr int KP = DK + 4, SP = VS + 8, AP = C + 4;
+  static_assert(DK % 16 == 0 && DK / 16 <= SCAN_THREADS / 32, "16 state rows per warp");
   extern __shared__ float sm[];
   float* sS = sm;               // [DK][SP]   state slice
   float* sW = sS + DK * SP;     // [C][KP]
@@ -351,8 +358,9 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int sl = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int c0 = sl * VS;
+  const int r0 = (warp & 3) * 16, n0 = (warp >> 2) * 16;  // rows / columns of v_new and out
 
-  for (int i = tid; i < DK * VS; i += 128) {
+  for (int i = tid; i < DK * VS; i += SCAN_THREADS) {
     const int d = i / VS, c = i % VS;
     sS[d * SP + c] = p.s_in ? p.s_in[b * p.s_bs + ((size_t)h * DK + d) * DV + c0 + c] : 0.f;
   }
@@ -364,19 +372,19 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
       const float* w = p.w + ci * C * DK;
       const float* q = p.qp + ci * C * DK;
       const float* k = p.kp + ci * C * DK;
-      for (int i = tid; i < C * DK / 4; i += 128) {
+      for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
         const int r = (i * 4) / DK, d = (i * 4) % DK;
         cp_async16(sW + r * KP + d, w + 4 * i);
         cp_async16(sQp + r * KP + d, q + 4 * i);
         cp_async16(sKp + r * KP + d, k + 4 * i);
       }
       const float* u = p.u + ci * C * DV + c0;
-      for (int i = tid; i < C * VS / 4; i += 128) {
+      for (int i = tid; i < C * VS / 4; i += SCAN_THREADS) {
         const int r = (i * 4) / VS, c = (i * 4) % VS;
         cp_async16(sU + r * SP + c, u + r * DV + c);
       }
       const float* in = p.intra + ci * C * C;
-      for (int i = tid; i < C * C / 4; i += 128) {
+      for (int i = tid; i < C * C / 4; i += SCAN_THREADS) {
         const int r = (i * 4) / C, c = (i * 4) % C;
         cp_async16(sI + r * AP + c, in + 4 * i);
       }
@@ -384,30 +392,29 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
     }
     const float el = p.elast[ci];
     __syncthreads();
-    const int r0 = warp * 16;
-    float vn[4][4], o[4][4];
+    float vn[2][4], o[2][4];
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) vn[n][e] = o[n][e] = 0.f;
     // W S and q' S over dk
-#pragma unroll 1
+#pragma unroll 2
     for (int k0 = 0; k0 < DK; k0 += 8) {
       const Frag<true> fw = frag_a<true>(sW, KP, r0, k0, gid, tig);
       const Frag<true> fq = frag_a<true>(sQp, KP, r0, k0, gid, tig);
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        const Frag<true> fs = frag_b<true>(sS, SP, k0, n * 8, gid, tig);
+      for (int n = 0; n < 2; ++n) {
+        const Frag<true> fs = frag_b<true>(sS, SP, k0, n0 + n * 8, gid, tig);
         mma<true>(vn[n], fw, fs);
         mma<true>(o[n], fq, fs);
       }
     }
-    // v_new = U - W S (in place over U: each warp owns its 16 rows)
+    // v_new = U - W S (in place over U: each warp owns its 16 x 16 block)
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int i = r0 + gid + (e >> 1) * 8, j = n * 8 + 2 * tig + (e & 1);
+        const int i = r0 + gid + (e >> 1) * 8, j = n0 + n * 8 + 2 * tig + (e & 1);
         sU[i * SP + j] -= vn[n][e];
       }
     __syncthreads();
@@ -416,24 +423,23 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
     for (int k0 = 0; k0 < r0 + 16; k0 += 8) {
       const Frag<true> fi = frag_a<true>(sI, AP, r0, k0, gid, tig);
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        const Frag<true> fv = frag_b<true>(sU, SP, k0, n * 8, gid, tig);
+      for (int n = 0; n < 2; ++n) {
+        const Frag<true> fv = frag_b<true>(sU, SP, k0, n0 + n * 8, gid, tig);
         mma<true>(o[n], fi, fv);
       }
     }
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int hlf = 0; hlf < 2; ++hlf) {
         const int t = ch * C + r0 + gid + hlf * 8;
         if (t < p.T)
-          *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n * 8 + 2 * tig) =
+          *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n0 + n * 8 + 2 * tig) =
               make_float2(o[n][2 * hlf], o[n][2 * hlf + 1]);
       }
-    // S = e^last S + k'^T v_new: warp w owns state rows 32w .. 32w+31
-#pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      const int d0 = warp * 32 + m * 16;
+    // S = e^last S + k'^T v_new: warp w owns state rows 16 w .. 16 w + 15
+    if (warp < DK / 16) {
+      const int d0 = warp * 16;
       float acc[4][4];
 #pragma unroll
       for (int n = 0; n < 4; ++n)
@@ -442,7 +448,7 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
           const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
           acc[n][e] = sS[d * SP + c] * el;
         }
-#pragma unroll 1
+#pragma unroll 2
       for (int k0 = 0; k0 < C; k0 += 8) {
         const Frag<true> fk = frag_at<true>(sKp, KP, d0, k0, gid, tig);
 #pragma unroll
@@ -462,7 +468,7 @@ __global__ void __launch_bounds__(128) gdn_scan_kernel(Params p) {
   }
   __syncthreads();
   if (p.s_out)
-    for (int i = tid; i < DK * VS; i += 128) {
+    for (int i = tid; i < DK * VS; i += SCAN_THREADS) {
       const int d = i / VS, c = i % VS;
       p.s_out[(size_t)b * p.nv * DK * DV + ((size_t)h * DK + d) * DV + c0 + c] = sS[d * SP + c];
     }
@@ -491,7 +497,7 @@ int launch(const Params& p, cudaStream_t st) {
   gdn_prep_kernel<DK, DV><<<dim3(p.n_chunks, p.nv, p.B), 128, prep_smem<DK, DV>(), st>>>(p);
   int rc = check_launch("gdn_prep_kernel");
   if (rc) return rc;
-  gdn_scan_kernel<DK, DV><<<dim3(DV / VS, p.nv, p.B), 128, scan_smem<DK, DV>(), st>>>(p);
+  gdn_scan_kernel<DK, DV><<<dim3(DV / VS, p.nv, p.B), SCAN_THREADS, scan_smem<DK, DV>(), st>>>(p);
   return check_launch("gdn_scan_kernel");
 }
 
