@@ -4,20 +4,18 @@
 // replacing depthwise_conv1d's K shifted full-tensor passes plus the
 // narrow / mul / cat copies (decoder.rs:137-151) with one HBM pass.
 //
-// One thread per (row, token, 8 channels): 16-byte loads across channels
-// are coalesced; the K-1 earlier tokens a thread also reads were read by the
-// neighbouring tokens' threads and come from L2.  The tail is read in place
-// (batch stride 0 broadcasts one prefix state to every row) and the new tail
-// is written by the threads of the last token.
+// One thread per (row, run of R tokens, 8 channels): every input row of the
+// run and its K-1 earlier tokens is loaded once, all loads in flight before
+// the first use (16 or 32 bytes per row and thread, coalesced across the
+// channel groups of a warp); weights are loaded once per thread; each output
+// row is one 16- or 32-byte store.  The tail is read in place (batch stride
+// 0 broadcasts one prefix state to every row) and the new tail is written by
+// the thread whose run holds the last token.
 #include "common.cuh"
 
 namespace cevk {
 
-template <typename T>
-__device__ __forceinline__ void ld8(const T* p, float* f) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = to_f(p[i]);
-}
+// 8 consecutive elements <-> f32 (16-byte aligned for bf16, 32 for f32).
 __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* f) {
   const uint4 u = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -28,73 +26,104 @@ __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* f) {
     f[2 * i + 1] = v.y;
   }
 }
+__device__ __forceinline__ void ld8(const float* p, float* f) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+__device__ __forceinline__ void st8(__nv_bfloat16* p, const float* f) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void st8(float* p, const float* f) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
+constexpr int CONV_RUN = 4;  // tokens per thread
 
 // GATED: y = c * (bias + sum_k w_k * (b*x)[t-K+1+k]); else y = silu(sum_k w_k * x[t-K+1+k]).
 template <typename T, bool GATED, int K>
-__global__ void __launch_bounds__(256) causal_conv_kernel(const T* __restrict__ in, int in_row, const T* __restrict__ w,
+__global__ void __launch_bounds__(256, 2) causal_conv_kernel(const T* __restrict__ in, int in_row, const T* __restrict__ w,
                                                           const T* __restrict__ bias, const T* __restrict__ tail_in,
                                                           long long tail_bs, T* __restrict__ tail_out,
                                                           T* __restrict__ y, int B, int Tn, int C) {
-  const int groups = C / 8;
-  const long long total = (long long)B * Tn * groups;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int g = (int)(i % groups);
-    const long long bt = i / groups;
-    const int t = (int)(bt % Tn);
-    const int b = (int)(bt / Tn);
-    const int ch0 = g * 8;
-    // window[k] = input of token t-K+1+k (gated: b*x, rounded like the
-    // reference's model-dtype product)
-    float win[K][8];
+  constexpr int R = CONV_RUN, NW = R + K - 1;
+  const int groups = C / 8, runs = (Tn + R - 1) / R;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * runs * groups) return;
+  const int g = (int)(i % groups);
+  const int br = (int)(i / groups);
+  const int run = br % runs, b = br / runs;
+  const int ch0 = g * 8, t0 = run * R;
+  // window row r = input of token t0 - (K-1) + r (gated: b*x, rounded like
+  // the reference's model-dtype product)
+  float win[NW][8];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int tt = t - (K - 1) + k;
-      if (tt >= 0) {
-        const T* row = in + ((long long)b * Tn + tt) * in_row;
-        if (GATED) {
-          float bb[8], xx[8];
-          ld8(row + ch0, bb);
-          ld8(row + 2 * C + ch0, xx);
+  for (int r = 0; r < NW; ++r) {
+    const int tt = t0 - (K - 1) + r;
+    if (tt >= 0 && tt < Tn) {
+      const T* row = in + ((long long)b * Tn + tt) * in_row;
+      if (GATED) {
+        float bb[8];
+        ld8(row + ch0, bb);
+        ld8(row + 2 * C + ch0, win[r]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) win[k][j] = to_f(from_f<T>(bb[j] * xx[j]));
-        } else {
-          ld8(row + ch0, win[k]);
-        }
+        for (int j = 0; j < 8; ++j) win[r][j] = to_f(from_f<T>(bb[j] * win[r][j]));
       } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          win[k][j] = tail_in ? to_f(tail_in[b * tail_bs + (long long)(ch0 + j) * (K - 1) + (K - 1 + tt)]) : 0.f;
+        ld8(row + ch0, win[r]);
       }
+    } else if (tt < 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        win[r][j] = tail_in ? to_f(tail_in[b * tail_bs + (long long)(ch0 + j) * (K - 1) + (K - 1 + tt)]) : 0.f;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) win[r][j] = 0.f;
     }
+  }
+  // the group's 8 x K weights are contiguous: K vector loads of 8
+  float wk[8 * K], bs[8];
+#pragma unroll
+  for (int k = 0; k < K; ++k) ld8(w + ch0 * K + 8 * k, wk + 8 * k);
+  if (GATED && bias) ld8(bias + ch0, bs);
+  else
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bs[j] = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int t = t0 + r;
+    if (t >= Tn) break;
     float out[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float acc = 0.f;
 #pragma unroll
-      for (int k = 0; k < K; ++k) acc += to_f(w[(ch0 + j) * K + k]) * win[k][j];
-      if (GATED) {
-        if (bias) acc += to_f(bias[ch0 + j]);
-        out[j] = acc;
-      } else {
-        out[j] = acc / (1.f + __expf(-acc));
-      }
+      for (int k = 0; k < K; ++k) acc += wk[j * K + k] * win[r + k][j];
+      out[j] = GATED ? acc + bs[j] : acc / (1.f + __expf(-acc));
     }
     T* yr = y + ((long long)b * Tn + t) * C + ch0;
     if (GATED) {
       float cc[8];
       ld8(in + ((long long)b * Tn + t) * in_row + C + ch0, cc);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) yr[j] = from_f<T>(cc[j] * to_f(from_f<T>(out[j])));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) yr[j] = from_f<T>(out[j]);
+      for (int j = 0; j < 8; ++j) out[j] = cc[j] * to_f(from_f<T>(out[j]));
     }
-    if (tail_out && t == Tn - 1) {
-      // new tail = the last K-1 inputs of [tail | sequence]: window[1..K-1]
+    st8(yr, out);
+  }
+  if (tail_out && t0 <= Tn - 1 && Tn - 1 < t0 + R) {
+    // new tail = the last K-1 inputs of [tail | sequence]: tokens Tn-K+1 .. Tn-1
 #pragma unroll
-      for (int k = 1; k < K; ++k)
+    for (int k = 0; k < K - 1; ++k) {
+      const int r = Tn - t0 + k;  // window row of token Tn-K+1+k
 #pragma unroll
-        for (int j = 0; j < 8; ++j) tail_out[((long long)b * C + ch0 + j) * (K - 1) + (k - 1)] = from_f<T>(win[k][j]);
+      for (int rr = 0; rr < NW; ++rr)
+        if (rr == r)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) tail_out[((long long)b * C + ch0 + j) * (K - 1) + k] = from_f<T>(win[rr][j]);
     }
   }
 }
@@ -102,13 +131,15 @@ __global__ void __launch_bounds__(256) causal_conv_kernel(const T* __restrict__ 
 template <typename T, bool GATED>
 static int launch_conv(const void* in, int in_row, const void* w, const void* bias, const void* tail_in, long long tbs,
                        void* tail_out, void* y, int B, int Tn, int C, int K, cudaStream_t st) {
-  const long long total = (long long)B * Tn * (C / 8);
-  long long blocks = (total + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  if (blocks < 1) blocks = 1;
-#define L(KK)                                                                                                      \
-  causal_conv_kernel<T, GATED, KK><<<(unsigned)blocks, 256, 0, st>>>((const T*)in, in_row, (const T*)w, (const T*)bias, \
-                                                                     (const T*)tail_in, tbs, (T*)tail_out, (T*)y, B, Tn, C)
+  if (((uintptr_t)in | (uintptr_t)y | (uintptr_t)w | (uintptr_t)bias) & (8 * sizeof(T) - 1))
+    return set_error(CEVK_E_SHAPE, "conv: input, output, weights and bias must be %d-byte aligned",
+                     (int)(8 * sizeof(T)));
+  const long long total = (long long)B * ((Tn + CONV_RUN - 1) / CONV_RUN) * (C / 8);
+  if (total > (1ll << 31)) return set_error(CEVK_E_SHAPE, "conv: %lld thread jobs", total);
+  const unsigned blocks = (unsigned)((total + 255) / 256);
+#define L(KK)                                                                                                 \
+  causal_conv_kernel<T, GATED, KK><<<blocks, 256, 0, st>>>((const T*)in, in_row, (const T*)w, (const T*)bias, \
+                                                           (const T*)tail_in, tbs, (T*)tail_out, (T*)y, B, Tn, C)
   switch (K) {
     case 2: L(2); break;
     case 3: L(3); break;
