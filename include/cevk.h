@@ -179,8 +179,11 @@ int cevk_gdn_conv(const void* mixed, int32_t mixed_row_stride, const void* conv_
  *   y: [B, T, nv*dv].
  * Padding tokens at the end of a row are computed like the reference
  * (causal: they never reach a real token); s_out is the state after all T
- * tokens.  workspace: device scratch of cevk_gdn_workspace_size() bytes
- * (the f32 core output before the norm). */
+ * tokens.  workspace: device scratch of cevk_gdn_workspace_size() bytes:
+ * the f32 core output before the norm and, for bf16 with dk = dv = 64 or
+ * 128, the per-chunk matrices of the tensor-core path.  A workspace of only
+ * B*T*nv*dv*4 bytes (the core output) runs every dtype on the f32 SIMT
+ * kernel instead. */
 size_t cevk_gdn_workspace_size(int32_t B, int32_t T, int32_t nv, int32_t dk, int32_t dv);
 int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride, const void* z,
                            int32_t z_row_stride, const float* a_log, const float* dt_bias, const void* norm_w,
@@ -195,8 +198,10 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
  * cevk_gdn_chunk_prefill without workspace / workspace_bytes; the f32
  * scratch is a fixed device array inside the library (CEVK_GDN_NOALLOC_MAX_BYTES,
  * held by every GPU that loads the library until exit).
- *   - Calls needing more scratch (B*T*nv*dv*4 bytes) than the array holds
- *     return CEVK_E_SHAPE; split them or use the workspace entry point.
+ *   - The array holds cevk_gdn_workspace_size() for small calls (tensor-core
+ *     path); larger ones run the f32 SIMT kernel, whose scratch is
+ *     B*T*nv*dv*4 bytes.  Calls needing more than that return CEVK_E_SHAPE;
+ *     split them or use the workspace entry point.
  *   - The first call on a device looks up the array's device address (once
  *     per device, with that device current); make that first call before
  *     any stream capture.

@@ -299,9 +299,13 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
     return set_error(CEVK_E_SHAPE, "gdn: heads %d/%d, dk %d, dv %d unsupported", nk, nv, dk, dv);
   if (C != 2 * nk * dk + nv * dv) return set_error(CEVK_E_SHAPE, "gdn: C %d != 2*nk*dk + nv*dv", C);
   if (B <= 0 || T <= 0) return CEVK_OK;
-  const size_t need = cevk_gdn_workspace_size(B, T, nv, dk, dv);
-  if (!workspace || workspace_bytes < need)
-    return set_error(CEVK_E_SHAPE, "gdn: workspace of %zu bytes needed (got %zu)", need, workspace_bytes);
+  // A workspace of cevk_gdn_workspace_size() bytes runs bf16 on the tensor
+  // cores; one that holds only the f32 core output runs the SIMT kernel.
+  const size_t need_core = (size_t)B * T * nv * dv * sizeof(float);
+  if (!workspace || workspace_bytes < need_core)
+    return set_error(CEVK_E_SHAPE, "gdn: workspace of %zu bytes needed (got %zu)",
+                     cevk_gdn_workspace_size(B, T, nv, dk, dv), workspace_bytes);
+  const bool full_ws = workspace_bytes >= cevk_gdn_workspace_size(B, T, nv, dk, dv);
   GdnParams prm;
   prm.conv = conv_out;
   prm.Cc = C;
@@ -326,7 +330,7 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
   const unsigned ng = (unsigned)((rows * nv + 7) / 8);
   if (dtype == CEVK_BF16) {
     int rc;
-    if (gdn_tc_supported(dk, dv) && ((uintptr_t)conv_out & 15) == 0 && C % 8 == 0) {
+    if (full_ws && gdn_tc_supported(dk, dv) && ((uintptr_t)conv_out & 15) == 0 && C % 8 == 0) {
       // tensor cores (gdn_tc.cu): chunk-parallel prep + state scan
       rc = gdn_tc_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,
                       nk, nv, dk, dv, st);
@@ -401,7 +405,9 @@ extern "C" int cevk_gdn_chunk_prefill_noalloc(const void* conv_out, int32_t C, c
                                               int32_t nk, int32_t nv, int32_t dk, int32_t dv, int32_t dtype,
                                               void* stream) {
   if (B <= 0 || T <= 0) return CEVK_OK;
-  const size_t need = cevk_gdn_workspace_size(B, T, nv, dk, dv);
+  // The array runs the tensor-core path when its scratch fits, else the SIMT
+  // kernel, whose scratch is the f32 core output alone.
+  const size_t need = (size_t)B * T * nv * dv * sizeof(float);
   if (need > cevk::kGdnStaticScratchBytes)
     return cevk::set_error(CEVK_E_SHAPE,
                            "gdn noalloc: %d rows x %d tokens x %d heads x %d columns need %zu bytes of scratch, "

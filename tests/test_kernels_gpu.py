@@ -284,13 +284,19 @@ def gdn_oracle(conv_out, ab, z, a_log, dt_bias, norm_w, s0, nk, nv, dk, dv, eps=
 
 @pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-4)])
 @pytest.mark.parametrize("B,T,with_state", [(1, 150, True), (3, 64, True), (2, 10, False)])
-def test_gdn_chunk_prefill_matches_oracle(dtype, tol, B, T, with_state):
+@pytest.mark.parametrize("ws_kind", ["full", "core"])
+@pytest.mark.parametrize("dk", [64, 128])
+def test_gdn_chunk_prefill_matches_oracle(dtype, tol, B, T, with_state, ws_kind, dk):
+    """bf16 with a full workspace runs the tensor-core kernels; a workspace
+    holding only the f32 core output runs the SIMT kernel (f32 always does).
+    dk = dv = 128 is the cfg4 head shape."""
     from cev_b200 import ops
-    nk, nv, dk, dv = 2, 4, 64, 64
+    nk, nv, dv = 2, 4, dk
     conv_out, ab, z, a_log, dt_bias, norm_w, s0 = gdn_inputs(B, T, nk, nv, dk, dv, dtype, 11)
     s_in = s0.cuda() if with_state else None
     s_out = torch.empty(B, nv, dk, dv, device="cuda")
-    ws = torch.empty(ops.gdn_workspace_size(B, T, nv, dk, dv), dtype=torch.uint8, device="cuda")
+    size = ops.gdn_workspace_size(B, T, nv, dk, dv) if ws_kind == "full" else B * T * nv * dv * 4
+    ws = torch.empty(size, dtype=torch.uint8, device="cuda")
     y = ops.gdn_chunk_prefill(conv_out.reshape(B * T, -1).cuda(), ab.reshape(B * T, -1).cuda(), 2 * nv,
                               z.reshape(B * T, -1).cuda(), nv * dv, a_log.cuda(), dt_bias.cuda(), norm_w.cuda(), 1e-6,
                               s_in, s_out, B, T, nk, nv, dk, dv, ws)
