@@ -228,20 +228,31 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     state in 512-token chunks, 64 questions of 64 tokens): the state is
     prefilled once into the cached prefix state, the questions run as
     right-padded rows continuing it (hybrid.rs:697-739).  4 option codes,
-    2 rotations per question (cfg4) / none (cfg5).  Decisions/s end to end."""
+    2 rotations per question (cfg4) / none (cfg5).  Decisions/s end to end.
+    With N > 1 GPUs cfg4 runs its own requests on every rank; cfg5 runs one
+    request stream on all ranks with the attention layers split by KV-head
+    group (one NCCL all-gather of head outputs per attention layer)."""
     import torch
     from cev_b200 import configs, hybrid, service, weights, workloads
     cfg = configs.get(name)
     seed, plen, nq, lo, hi, mode = (2, 16384, 32, 32, 128, "permute") if name == "cfg4" else (3, 65536, 64, 64, 64, "none")
+    rank = int(os.environ.get("RANK", "0"))
+    split = None
+    if name == "cfg5" and world > 1:
+        from cev_b200.tp import KvHeadSplit
+        split = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"],
+                            cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"], rank, world)
     w = weights.init_weights(cfg, seed, torch.bfloat16, dev)
-    dec = (hybrid.Qwen35 if name == "cfg4" else hybrid.Lfm2)(cfg, w, torch.bfloat16, dev, max_len=plen + 1024,
-                                                             arena_rows=plen + 8192)
+    if name == "cfg4":
+        dec = hybrid.Qwen35(cfg, w, torch.bfloat16, dev, max_len=plen + 1024, arena_rows=plen + 8192)
+    else:
+        dec = hybrid.Lfm2(cfg, w, torch.bfloat16, dev, max_len=plen + 1024, arena_rows=plen + 8192, split=split)
     del w
     codes = workloads.code_ids(4)
     eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=512, pass_tokens=8192, prefix_cache_tokens=plen)
-    rank = int(os.environ.get("RANK", "0"))
     vocab = cfg["vocab_size"] - 1
-    reqs = [workloads.decision_request(20_000 * (rank + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]
+    stream = 0 if split is not None else rank  # a split model runs the same requests on every rank
+    reqs = [workloads.decision_request(20_000 * (stream + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]
 
     def one(prefix, qs):
         return service.run_debiased(eng, prefix, qs, mode, codes, workloads.SEP_ID, max_permutations=2)
@@ -259,8 +270,10 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     dt = torch.tensor([time.perf_counter() - t0], device=dev)
     if world > 1:
         dist_mod.all_reduce(dt, op=dist_mod.ReduceOp.MAX)
-    return {"value": nq * n_req * world / dt.item(), "unit": "decisions/s", "requests_per_gpu": n_req,
-            "seconds": dt.item(), "workload": f"{name}: {plen}-token state, {nq} questions, rows continuing the state"}
+    streams = 1 if split is not None else world
+    return {"value": nq * n_req * streams / dt.item(), "unit": "decisions/s", "requests_per_stream": n_req,
+            "seconds": dt.item(), "workload": f"{name}: {plen}-token state, {nq} questions, rows continuing the state",
+            "parallelism": f"kv-head split x{world}" if split is not None else f"dp{world}"}
 
 
 def timed(fn, steps, warmup, stream):

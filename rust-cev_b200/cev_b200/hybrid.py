@@ -50,7 +50,7 @@ class _HybridDecoder:
 
     plus_one = False
 
-    def __init__(self, cfg, dtype, device, max_len, arena_rows):
+    def __init__(self, cfg, dtype, device, max_len, arena_rows, split=None):
         self.cfg = cfg
         self.dtype = dtype
         self.device = torch.device(device)
@@ -58,10 +58,13 @@ class _HybridDecoder:
         self.hq = cfg["num_attention_heads"]
         self.hkv = cfg["num_key_value_heads"]
         self.D = cfg.get("head_dim") or self.hidden // self.hq
+        # attention heads this process computes (all, or its KV-head group)
+        self.split = split
+        self.hq_a, self.hkv_a = (self.hq, self.hkv) if split is None else (split.hq_l, split.hkv_l)
         self.n_layers = cfg["num_hidden_layers"]
         self.attn_layers = [i for i, t in enumerate(cfg["layer_types"]) if t == "full_attention"]
         self.arena_index = {l: j for j, l in enumerate(self.attn_layers)}
-        self.arena = KvArena(len(self.attn_layers), arena_rows, self.hkv, self.D, dtype, self.device)
+        self.arena = KvArena(len(self.attn_layers), arena_rows, self.hkv_a, self.D, dtype, self.device)
         self.max_len = min(max_len, cfg.get("max_position_embeddings", max_len))
 
     def _w(self, weights, name):
@@ -99,7 +102,7 @@ class _HybridDecoder:
                 pstart = 0 if state is None else state.start
                 segs = [(b * T, T, pstart, past, scratch + b * T) for b in range(B)]
             rows_t = torch.tensor(rows, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
-            plan = ops.AttnPlan(segs, n, self.arena.capacity, self.hq, self.hkv, self.D, self.dtype, dev)
+            plan = ops.AttnPlan(segs, n, self.arena.capacity, self.hq_a, self.hkv_a, self.D, self.dtype, dev)
         try:
             x = ops.embed(self.embed_w, ids)
             h = ops.rms_norm(x, self.layers[0]["ln1"], self.eps, self.plus_one)
@@ -126,7 +129,7 @@ class _HybridDecoder:
 
     def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot):
         T = h.shape[0]
-        hq, hkv, D = self.hq, self.hkv, self.D
+        hq, hkv, D = self.hq_a, self.hkv_a, self.D
         qkv = F.linear(h, L["qkv"])
         q = torch.empty(T, hq, D, dtype=self.dtype, device=self.device)
         j = self.arena_index[i]
@@ -215,8 +218,10 @@ class Lfm2(_HybridDecoder):
     """LFM2 causal decoder (lfm2.rs:270-431)."""
 
     def __init__(self, cfg: dict, weights: dict, dtype=torch.bfloat16, device="cuda", max_len=128000,
-                 arena_rows=65536 + 8192):
-        super().__init__(cfg, dtype, device, max_len, arena_rows)
+                 arena_rows=65536 + 8192, split=None):
+        """``split``: a :class:`cev_b200.tp.KvHeadSplit` to run the attention
+        layers on this rank's KV-head group (the other ranks hold the rest)."""
+        super().__init__(cfg, dtype, device, max_len, arena_rows, split)
         self.eps = cfg.get("norm_eps", 1e-5)
         self.theta = cfg.get("rope_theta") or (cfg.get("rope_parameters") or {}).get("rope_theta") or 1e6
         self.K = cfg.get("conv_L_cache", 3)
@@ -232,9 +237,9 @@ class Lfm2(_HybridDecoder):
                      gu=torch.cat([w(f + "w1.weight"), w(f + "w3.weight")], 0).contiguous(), down=w(f + "w2.weight"))
             if cfg["layer_types"][i] == "full_attention":
                 s = p + "self_attn."
+                qkv = torch.cat([w(s + "q_proj.weight"), w(s + "k_proj.weight"), w(s + "v_proj.weight")], 0)
                 L.update(kind="attn",
-                         qkv=torch.cat([w(s + "q_proj.weight"), w(s + "k_proj.weight"), w(s + "v_proj.weight")],
-                                       0).contiguous(),
+                         qkv=qkv.contiguous() if split is None else split.slice_fused_qkv(qkv),
                          qn=w(s + "q_layernorm.weight"), kn=w(s + "k_layernorm.weight"), o=w(s + "out_proj.weight"))
             else:
                 c = p + "conv."
@@ -245,10 +250,14 @@ class Lfm2(_HybridDecoder):
         self.norm_w = w("model.embedding_norm.weight")
 
     def _attn(self, i, L, h, pos_t, rows_t, plan):
-        """lfm2.rs:145-171."""
-        hq, hkv, D = self.hq, self.hkv, self.D
+        """lfm2.rs:145-171; with a KV-head split, this rank's heads and one
+        all-gather of the head outputs before the output projection."""
+        hq, hkv, D = self.hq_a, self.hkv_a, self.D
         _, ctx = self._attn_common(i, L, h, pos_t, rows_t, plan, (0, D), hq * D, (hq + hkv) * D, D)
-        return F.linear(ctx.view(h.shape[0], hq * D), L["o"])
+        ctx = ctx.view(h.shape[0], hq * D)
+        if self.split is not None:
+            ctx = self.split.gather(ctx)
+        return F.linear(ctx, L["o"])
 
     def _conv(self, i, L, h, B, T, state, keep):
         """ShortConv::forward (lfm2.rs:199-219)."""

@@ -1,0 +1,73 @@
+"""The LFM2 attention layers split by KV-head group over 2 GPUs (NCCL
+all-gather of head outputs) against the unsplit model on one GPU: same
+request, f32, readouts within 1e-4.  Needs 2 GPUs (skipped otherwise)."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _request(cfg):
+    from cev_b200 import workloads
+    codes = workloads.code_ids(3)
+    prefix, qs = workloads.decision_request(9, 300, 4, 14, 28, 3, cfg["vocab_size"])
+    return codes, prefix, [q.render(codes, workloads.SEP_ID) for q in qs]
+
+
+def _run(model, cfg):
+    from cev_b200 import hybrid
+    from cev_b200.engine import Request
+    codes, prefix, sfx = _request(cfg)
+    eng = hybrid.HybridEngine(model, codes, pad_id=0, prefill_chunk=128, pass_tokens=256)
+    out = eng.run(Request(prefix, sfx, [3] * len(sfx)))
+    return torch.stack([r.logits.float().cpu() for r in out.readouts])
+
+
+def _rank(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=timedelta(seconds=60))
+    try:
+        from cev_b200 import configs, hybrid, weights
+        from cev_b200.tp import KvHeadSplit
+        cfg = configs.tiny_lfm2()
+        w = weights.init_weights(cfg, 41)
+        D = cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"]
+        sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
+        split = _run(hybrid.Lfm2(cfg, w, torch.float32, f"cuda:{rank}", arena_rows=4096, split=sp), cfg)
+        err = None
+        if rank == 0:
+            whole = _run(hybrid.Lfm2(cfg, w, torch.float32, "cuda:0", arena_rows=4096), cfg)
+            err = (split - whole).abs().max().item()
+        dist.barrier()
+        q.put((rank, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_lfm2_kv_head_split_matches_unsplit():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    res = dict(q.get(timeout=10) for _ in range(2))
+    assert res[0] is not None and res[0] < 1e-4, res
