@@ -15,22 +15,7 @@
 
 namespace cevk {
 
-// 8 consecutive elements <-> f32 (16-byte aligned for bf16, 32 for f32).
-__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* f) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 v = __bfloat1622float2(h[i]);
-    f[2 * i] = v.x;
-    f[2 * i + 1] = v.y;
-  }
-}
-__device__ __forceinline__ void ld8(const float* p, float* f) {
-  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
+// f32 -> 8 consecutive elements (16-byte aligned for bf16, 32 for f32).
 __device__ __forceinline__ void st8(__nv_bfloat16* p, const float* f) {
   uint4 u;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
@@ -45,54 +30,91 @@ __device__ __forceinline__ void st8(float* p, const float* f) {
 
 constexpr int CONV_RUN = 4;  // tokens per thread
 
+// 8 elements in their storage form (one 16-byte vector for bf16, two for f32).
+template <typename T>
+struct Raw8 {
+  uint4 a, b;
+};
+template <typename T>
+__device__ __forceinline__ Raw8<T> ldraw(const T* p) {
+  Raw8<T> r;
+  r.a = *reinterpret_cast<const uint4*>(p);
+  if (sizeof(T) == 4) r.b = *reinterpret_cast<const uint4*>(p + 16 / sizeof(T));
+  return r;
+}
+__device__ __forceinline__ void unraw(const Raw8<__nv_bfloat16>& r, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r.a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __bfloat1622float2(h[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+__device__ __forceinline__ void unraw(const Raw8<float>& r, float* f) {
+  f[0] = __uint_as_float(r.a.x); f[1] = __uint_as_float(r.a.y); f[2] = __uint_as_float(r.a.z); f[3] = __uint_as_float(r.a.w);
+  f[4] = __uint_as_float(r.b.x); f[5] = __uint_as_float(r.b.y); f[6] = __uint_as_float(r.b.z); f[7] = __uint_as_float(r.b.w);
+}
+
 // GATED: y = c * (bias + sum_k w_k * (b*x)[t-K+1+k]); else y = silu(sum_k w_k * x[t-K+1+k]).
+// Every global load of the run is issued before any is used: token indices
+// are clamped into the row so that no load sits behind a branch, and rows
+// outside the sequence are replaced afterwards (tail state or zero).
 template <typename T, bool GATED, int K>
 __global__ void __launch_bounds__(256, 2) causal_conv_kernel(const T* __restrict__ in, int in_row, const T* __restrict__ w,
-                                                          const T* __restrict__ bias, const T* __restrict__ tail_in,
-                                                          long long tail_bs, T* __restrict__ tail_out,
-                                                          T* __restrict__ y, int B, int Tn, int C) {
+                                                             const T* __restrict__ bias, const T* __restrict__ tail_in,
+                                                             long long tail_bs, T* __restrict__ tail_out,
+                                                             T* __restrict__ y, int B, int Tn, int C) {
   constexpr int R = CONV_RUN, NW = R + K - 1;
   const int groups = C / 8, runs = (Tn + R - 1) / R;
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)B * runs * groups) return;
-  const int g = (int)(i % groups);
-  const int br = (int)(i / groups);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // < 2^31 (checked on the host)
+  if (i >= B * runs * groups) return;
+  const int g = i % groups, br = i / groups;
   const int run = br % runs, b = br / runs;
   const int ch0 = g * 8, t0 = run * R;
+  const T* rows = in + (long long)b * Tn * in_row;
+  Raw8<T> rx[NW], rb[GATED ? NW : 1], rc[GATED ? R : 1];
+#pragma unroll
+  for (int r = 0; r < NW; ++r) {
+    const int tt = min(max(t0 - (K - 1) + r, 0), Tn - 1);
+    const T* row = rows + (long long)tt * in_row;
+    if (GATED) {
+      rb[r] = ldraw(row + ch0);
+      rx[r] = ldraw(row + 2 * C + ch0);
+    } else {
+      rx[r] = ldraw(row + ch0);
+    }
+  }
+  if (GATED)
+#pragma unroll
+    for (int r = 0; r < R; ++r) rc[r] = ldraw(rows + (long long)min(t0 + r, Tn - 1) * in_row + C + ch0);
+  // the group's 8 x K weights are contiguous: K vector loads of 8
+  float wk[8 * K], bs[8];
+#pragma unroll
+  for (int k = 0; k < K; ++k) unraw(ldraw(w + ch0 * K + 8 * k), wk + 8 * k);
+  if (GATED && bias) unraw(ldraw(bias + ch0), bs);
+  else
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bs[j] = 0.f;
   // window row r = input of token t0 - (K-1) + r (gated: b*x, rounded like
   // the reference's model-dtype product)
   float win[NW][8];
 #pragma unroll
   for (int r = 0; r < NW; ++r) {
     const int tt = t0 - (K - 1) + r;
-    if (tt >= 0 && tt < Tn) {
-      const T* row = in + ((long long)b * Tn + tt) * in_row;
-      if (GATED) {
-        float bb[8];
-        ld8(row + ch0, bb);
-        ld8(row + 2 * C + ch0, win[r]);
+    unraw(rx[r], win[r]);
+    if (GATED) {
+      float bb[8];
+      unraw(rb[r], bb);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) win[r][j] = to_f(from_f<T>(bb[j] * win[r][j]));
-      } else {
-        ld8(row + ch0, win[r]);
-      }
-    } else if (tt < 0) {
+      for (int j = 0; j < 8; ++j) win[r][j] = to_f(from_f<T>(bb[j] * win[r][j]));
+    }
+    if (tt < 0) {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         win[r][j] = tail_in ? to_f(tail_in[b * tail_bs + (long long)(ch0 + j) * (K - 1) + (K - 1 + tt)]) : 0.f;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) win[r][j] = 0.f;
     }
   }
-  // the group's 8 x K weights are contiguous: K vector loads of 8
-  float wk[8 * K], bs[8];
-#pragma unroll
-  for (int k = 0; k < K; ++k) ld8(w + ch0 * K + 8 * k, wk + 8 * k);
-  if (GATED && bias) ld8(bias + ch0, bs);
-  else
-#pragma unroll
-    for (int j = 0; j < 8; ++j) bs[j] = 0.f;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int t = t0 + r;
@@ -105,14 +127,13 @@ __global__ void __launch_bounds__(256, 2) causal_conv_kernel(const T* __restrict
       for (int k = 0; k < K; ++k) acc += wk[j * K + k] * win[r + k][j];
       out[j] = GATED ? acc + bs[j] : acc / (1.f + __expf(-acc));
     }
-    T* yr = y + ((long long)b * Tn + t) * C + ch0;
     if (GATED) {
       float cc[8];
-      ld8(in + ((long long)b * Tn + t) * in_row + C + ch0, cc);
+      unraw(rc[r], cc);
 #pragma unroll
       for (int j = 0; j < 8; ++j) out[j] = cc[j] * to_f(from_f<T>(out[j]));
     }
-    st8(yr, out);
+    st8(y + ((long long)b * Tn + t) * C + ch0, out);
   }
   if (tail_out && t0 <= Tn - 1 && Tn - 1 < t0 + R) {
     // new tail = the last K-1 inputs of [tail | sequence]: tokens Tn-K+1 .. Tn-1
@@ -135,7 +156,7 @@ static int launch_conv(const void* in, int in_row, const void* w, const void* bi
     return set_error(CEVK_E_SHAPE, "conv: input, output, weights and bias must be %d-byte aligned",
                      (int)(8 * sizeof(T)));
   const long long total = (long long)B * ((Tn + CONV_RUN - 1) / CONV_RUN) * (C / 8);
-  if (total > (1ll << 31)) return set_error(CEVK_E_SHAPE, "conv: %lld thread jobs", total);
+  if (total >= (1ll << 31) - 256) return set_error(CEVK_E_SHAPE, "conv: %lld thread jobs", total);
   const unsigned blocks = (unsigned)((total + 255) / 256);
 #define L(KK)                                                                                                 \
   causal_conv_kernel<T, GATED, KK><<<blocks, 256, 0, st>>>((const T*)in, in_row, (const T*)w, (const T*)bias, \
