@@ -177,6 +177,8 @@ int cevk_gdn_conv(const void* mixed, int32_t mixed_row_stride, const void* conv_
  *     state to every row; NULL = zero state); s_out: f32 [B, nv, dk, dv]
  *     or NULL (may alias s_in only when s_batch_stride is nv*dk*dv);
  *   y: [B, T, nv*dv].
+ * Shapes: nv a multiple of nk, dk a multiple of 32 in [64, 128], dv 64, 128
+ * or 256; z, norm_w, y and z's row stride aligned to dv/32 elements.
  * Padding tokens at the end of a row are computed like the reference
  * (causal: they never reach a real token); s_out is the state after all T
  * tokens.  workspace: device scratch of cevk_gdn_workspace_size() bytes:

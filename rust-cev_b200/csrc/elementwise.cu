@@ -51,53 +51,65 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // residual (optional) += add; out = rms_norm(residual or x) * (w or 1+w).
-template <typename T>
+// One block per row; the row stays in registers (V vectors of 8 per
+// thread), and every load is issued before the first use (columns past the
+// row are clamped and masked, so no load sits behind a branch).
+template <typename T, int V, bool RESID, bool OUT>
 __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, T* __restrict__ residual,
                                                        const T* __restrict__ add, const T* __restrict__ w,
                                                        T* __restrict__ out, int hidden, float eps, int plus_one) {
   __shared__ float red[32];
   const size_t row = (size_t)blockIdx.x * hidden;
-  const T* src = residual ? residual + row : x + row;
-  float ss = 0.f;
-  for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
-    float f[8];
-    load8(src + c, f);
-    if (residual) {
-      float a[8];
-      load8(add + row + c, a);
+  const T* src = RESID ? residual + row : x + row;
+  float f[V][8], a[V][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] += a[i];
-      round8<T>(f);  // the sum is a model-dtype tensor in the reference
-      store8(residual + row + c, f);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  for (int v = 0; v < V; ++v) {
+    const int c = min((v * 256 + (int)threadIdx.x) * 8, hidden - 8);
+    load8(src + c, f[v]);
+    if (RESID) load8(add + row + c, a[v]);
   }
-  if (!out) return;  // residual add only
-  const float r = rsqrtf(block_sum(ss, red) / hidden + eps);
-  for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
-    float f[8], g[8];
-    load8(src + c, f);
-    load8(w + c, g);
+  float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = f[i] * r * (g[i] + (plus_one ? 1.f : 0.f));
-    store8(out + row + c, f);
+  for (int v = 0; v < V; ++v) {
+    const int c = (v * 256 + threadIdx.x) * 8;
+    if (RESID) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[v][i] += a[v][i];
+      round8<T>(f[v]);  // the sum is a model-dtype tensor in the reference
+      if (c < hidden) store8(residual + row + c, f[v]);
+    }
+    if (c < hidden)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[v][i] * f[v][i];
+  }
+  if constexpr (OUT) {  // else: residual add only
+    float g[V][8];
+#pragma unroll
+    for (int v = 0; v < V; ++v) load8(w + min((v * 256 + (int)threadIdx.x) * 8, hidden - 8), g[v]);
+    const float r = rsqrtf(block_sum(ss, red) / hidden + eps);
+    const float one = plus_one ? 1.f : 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int c = (v * 256 + threadIdx.x) * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[v][i] = f[v][i] * r * (g[v][i] + one);
+      if (c < hidden) store8(out + row + c, f[v]);
+    }
   }
 }
 
+// One vector of 8 per thread: blockIdx.x over the row, blockIdx.y over rows.
 template <typename T>
-__global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int n, int inter) {
-  const long long per_row = inter / 8;
-  const long long total = (long long)n * per_row;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / per_row;
-    const int c = (int)(i % per_row) * 8;
+__global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int n, int inter) {
+  const int c = (blockIdx.x * 256 + threadIdx.x) * 8;
+  if (c >= inter) return;
+  for (int r = blockIdx.y; r < n; r += gridDim.y) {
     float g[8], u[8];
-    load8(gu + r * 2 * inter + c, g);
-    load8(gu + r * 2 * inter + inter + c, u);
+    load8(gu + (size_t)r * 2 * inter + c, g);
+    load8(gu + (size_t)r * 2 * inter + inter + c, u);
 #pragma unroll
     for (int j = 0; j < 8; ++j) g[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
-    store8(out + r * inter + c, g);
+    store8(out + (size_t)r * inter + c, g);
   }
 }
 
@@ -112,20 +124,21 @@ __global__ void embed_kernel(const T* __restrict__ table, const int32_t* __restr
   }
 }
 
+// One vector of 8 per thread: blockIdx.x over the token's heads x D,
+// blockIdx.y over tokens.
 template <typename T>
-__global__ void sigmoid_gate_kernel(const T* __restrict__ a, const T* __restrict__ gate, int grs, int ghs,
-                                    T* __restrict__ out, int n, int heads, int D) {
-  const long long total = (long long)n * heads * (D / 8);
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long t = i / (heads * (D / 8));
-    const int rem = (int)(i % (heads * (D / 8)));
-    const int h = rem / (D / 8), c = (rem % (D / 8)) * 8;
+__global__ void __launch_bounds__(256) sigmoid_gate_kernel(const T* __restrict__ a, const T* __restrict__ gate, int grs,
+                                                           int ghs, T* __restrict__ out, int n, int heads, int D) {
+  const int i = blockIdx.x * 256 + threadIdx.x;  // vector index within a token
+  if (i >= heads * (D / 8)) return;
+  const int h = i / (D / 8), c = (i % (D / 8)) * 8;
+  for (int t = blockIdx.y; t < n; t += gridDim.y) {
     float x[8], g[8];
-    load8(a + (t * heads + h) * D + c, x);
-    load8(gate + t * grs + (long long)h * ghs + c, g);
+    load8(a + ((size_t)t * heads + h) * D + c, x);
+    load8(gate + (size_t)t * grs + (size_t)h * ghs + c, g);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = x[j] * (1.f / (1.f + __expf(-g[j])));
-    store8(out + (t * heads + h) * D + c, x);
+    store8(out + ((size_t)t * heads + h) * D + c, x);
   }
 }
 
@@ -162,10 +175,6 @@ __global__ void __launch_bounds__(256) readout_kernel(const T* __restrict__ x, c
   }
 }
 
-static unsigned grid_for(long long work, int threads) {
-  long long b = (work + threads - 1) / threads;
-  return (unsigned)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
-}
 
 }  // namespace cevk
 
@@ -190,12 +199,29 @@ int cevk_rms_norm(const void* x, void* residual, const void* add, const void* w,
                   float eps, int32_t plus_one, int32_t dtype, void* stream) {
   if ((!x && !residual) || (residual && !add) || (out && !w) || (!out && !residual))
     return set_error(CEVK_E_SHAPE, "rms_norm: null pointer");
-  if (hidden % 8) return set_error(CEVK_E_SHAPE, "rms_norm: hidden %d not a multiple of 8", hidden);
+  if (hidden % 8 || hidden > 256 * 8 * 8)
+    return set_error(CEVK_E_SHAPE, "rms_norm: hidden %d (a multiple of 8, at most 16384)", hidden);
   if (n <= 0) return CEVK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define CALL rms_norm_kernel<T><<<n, 256, 0, st>>>((const T*)x, (T*)residual, (const T*)add, (const T*)w, (T*)out, hidden, eps, plus_one)
+  const int V = hidden <= 2048 ? 1 : hidden <= 4096 ? 2 : hidden <= 8192 ? 4 : 8;
+#define RN(VV, RS, OU)                                                                                       \
+  rms_norm_kernel<T, VV, RS, OU><<<n, 256, 0, st>>>((const T*)x, (T*)residual, (const T*)add, (const T*)w, \
+                                                    (T*)out, hidden, eps, plus_one)
+#define RNV(RS, OU)                    \
+  switch (V) {                         \
+    case 1: RN(1, RS, OU); break;      \
+    case 2: RN(2, RS, OU); break;      \
+    case 4: RN(4, RS, OU); break;      \
+    default: RN(8, RS, OU); break;     \
+  }
+#define CALL                                    \
+  if (residual && out) { RNV(true, true); }     \
+  else if (residual) { RNV(true, false); }      \
+  else { RNV(false, true); }
   CEVK_DISPATCH(dtype, CALL, CALL);
 #undef CALL
+#undef RNV
+#undef RN
   return check_launch("rms_norm_kernel");
 }
 
@@ -204,7 +230,7 @@ int cevk_swiglu(const void* gu, void* out, int32_t n, int32_t inter, int32_t dty
   if (inter % 8) return set_error(CEVK_E_SHAPE, "swiglu: inter %d not a multiple of 8", inter);
   if (n <= 0) return CEVK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned g = grid_for((long long)n * inter / 8, 256);
+  const dim3 g((unsigned)((inter / 8 + 255) / 256), (unsigned)(n < 65535 ? n : 65535));
 #define CALL swiglu_kernel<T><<<g, 256, 0, st>>>((const T*)gu, (T*)out, n, inter)
   CEVK_DISPATCH(dtype, CALL, CALL);
 #undef CALL
@@ -231,7 +257,7 @@ int cevk_sigmoid_gate(const void* a, const void* gate, int32_t gate_row_stride, 
     return set_error(CEVK_E_SHAPE, "sigmoid_gate: sizes must be multiples of 8");
   if (n <= 0) return CEVK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned g = grid_for((long long)n * heads * head_dim / 8, 256);
+  const dim3 g((unsigned)((heads * (head_dim / 8) + 255) / 256), (unsigned)(n < 65535 ? n : 65535));
 #define CALL sigmoid_gate_kernel<T><<<g, 256, 0, st>>>((const T*)a, (const T*)gate, gate_row_stride, gate_head_stride, (T*)out, n, heads, head_dim)
   CEVK_DISPATCH(dtype, CALL, CALL);
 #undef CALL

@@ -243,25 +243,76 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_kernel(GdnParams p) {
     }
 }
 
-template <typename T>
-__global__ void gdn_gated_norm_kernel(const float* __restrict__ core, const T* __restrict__ z, int z_rs,
-                                      const T* __restrict__ w, float eps, T* __restrict__ y, long long rows, int nv,
-                                      int dv) {
+// N consecutive 32-bit words in one or two vector accesses (N = 1, 2, 4, 8).
+template <int N>
+__device__ __forceinline__ void ldw(const void* p, uint32_t* w) {
+  if constexpr (N == 1) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else if constexpr (N == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+      w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+    }
+  }
+}
+template <int N>
+__device__ __forceinline__ void stw(void* p, const uint32_t* w) {
+  if constexpr (N == 1) {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i)
+      reinterpret_cast<uint4*>(p)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
+}
+
+// y = rmsnorm(o) * w * silu(z) per (token, head): one warp per row of dv =
+// 32 * E values, E consecutive values per lane, every load issued first.
+template <typename T, int E>
+__global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const float* __restrict__ core, const T* __restrict__ z,
+                                                             int z_rs, const T* __restrict__ w, float eps,
+                                                             T* __restrict__ y, long long rows, int nv, int dv) {
+  constexpr int WT = E * (int)sizeof(T) / 4;  // 32-bit words of E model-dtype values
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long job = (long long)blockIdx.x * (blockDim.x >> 5) + warp;  // (b*T + t) * nv + h
   if (job >= rows * nv) return;
   const long long bt = job / nv;
   const int h = (int)(job % nv);
-  const float* o = core + job * dv;
+  uint32_t ow[E], zw[WT], ww[WT];
+  ldw<E>(core + job * dv + lane * E, ow);
+  ldw<WT>(z + bt * z_rs + (long long)h * dv + lane * E, zw);
+  ldw<WT>(w + lane * E, ww);
+  const float* o = reinterpret_cast<const float*>(ow);
+  const T* zz = reinterpret_cast<const T*>(zw);
+  const T* wv = reinterpret_cast<const T*>(ww);
   float ss = 0.f;
-  for (int d = lane; d < dv; d += 32) ss += o[d] * o[d];
+#pragma unroll
+  for (int i = 0; i < E; ++i) ss += o[i] * o[i];
   ss = warp_sum(ss);
   const float r = 1.f / sqrtf(ss / dv + eps);
-  const T* zr = z + bt * z_rs + (long long)h * dv;
-  T* yr = y + bt * (long long)nv * dv + (long long)h * dv;
-  for (int d = lane; d < dv; d += 32) {
-    const float zz = to_f(zr[d]);
-    yr[d] = from_f<T>(o[d] * r * to_f(w[d]) * (zz / (1.f + expf(-zz))));
+  T out[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    const float zf = to_f(zz[i]);
+    out[i] = from_f<T>(o[i] * r * to_f(wv[i]) * (zf / (1.f + expf(-zf))));
+  }
+  stw<WT>(y + bt * (long long)nv * dv + (long long)h * dv + lane * E, reinterpret_cast<const uint32_t*>(out));
+}
+
+template <typename T>
+static void launch_gated_norm(const float* core, const T* z, int z_rs, const T* w, float eps, T* y, long long rows,
+                              int nv, int dv, cudaStream_t st) {
+  const unsigned ng = (unsigned)((rows * nv + 7) / 8);
+  switch (dv) {
+    case 64: gdn_gated_norm_kernel<T, 2><<<ng, 256, 0, st>>>(core, z, z_rs, w, eps, y, rows, nv, dv); break;
+    case 128: gdn_gated_norm_kernel<T, 4><<<ng, 256, 0, st>>>(core, z, z_rs, w, eps, y, rows, nv, dv); break;
+    default: gdn_gated_norm_kernel<T, 8><<<ng, 256, 0, st>>>(core, z, z_rs, w, eps, y, rows, nv, dv); break;
   }
 }
 
@@ -295,8 +346,14 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
                            size_t workspace_bytes, int32_t dtype, void* stream) {
   if (!conv_out || !ab || !z || !a_log || !dt_bias || !norm_w || !y)
     return set_error(CEVK_E_SHAPE, "gdn: null pointer");
-  if (nk <= 0 || nv % nk || dk % 32 || dk < 64 || dk > 128 || dv % GDVS || dv > 256)
+  if (nk <= 0 || nv % nk || dk % 32 || dk < 64 || dk > 128 || (dv != 64 && dv != 128 && dv != 256))
     return set_error(CEVK_E_SHAPE, "gdn: heads %d/%d, dk %d, dv %d unsupported", nk, nv, dk, dv);
+  {
+    // the gated norm reads dv/32 consecutive z / norm_w values per lane
+    const size_t vb = (size_t)(dv / 32) * (dtype == CEVK_BF16 ? 2 : 4);
+    if (((uintptr_t)z | (uintptr_t)norm_w | (uintptr_t)y) % vb || (z_row_stride * (dtype == CEVK_BF16 ? 2 : 4)) % vb)
+      return set_error(CEVK_E_SHAPE, "gdn: z, norm_w, y and the z row stride must be %zu-byte aligned", vb);
+  }
   if (C != 2 * nk * dk + nv * dv) return set_error(CEVK_E_SHAPE, "gdn: C %d != 2*nk*dk + nv*dv", C);
   if (B <= 0 || T <= 0) return CEVK_OK;
   // A workspace of cevk_gdn_workspace_size() bytes runs bf16 on the tensor
@@ -340,16 +397,15 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
       rc = check_launch("gdn_chunk_kernel");
     }
     if (rc) return rc;
-    gdn_gated_norm_kernel<__nv_bfloat16><<<ng, 256, 0, st>>>(prm.core, (const __nv_bfloat16*)z, z_row_stride,
-                                                             (const __nv_bfloat16*)norm_w, eps, (__nv_bfloat16*)y,
-                                                             rows, nv, dv);
+    launch_gated_norm<__nv_bfloat16>(prm.core, (const __nv_bfloat16*)z, z_row_stride, (const __nv_bfloat16*)norm_w,
+                                     eps, (__nv_bfloat16*)y, rows, nv, dv, st);
   } else if (dtype == CEVK_F32) {
     cudaFuncSetAttribute(gdn_chunk_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     gdn_chunk_kernel<float><<<grid, 256, smem, st>>>(prm);
     int rc = check_launch("gdn_chunk_kernel");
     if (rc) return rc;
-    gdn_gated_norm_kernel<float><<<ng, 256, 0, st>>>(prm.core, (const float*)z, z_row_stride, (const float*)norm_w,
-                                                     eps, (float*)y, rows, nv, dv);
+    launch_gated_norm<float>(prm.core, (const float*)z, z_row_stride, (const float*)norm_w, eps, (float*)y, rows, nv,
+                             dv, st);
   } else {
     return set_error(CEVK_E_UNSUPPORTED, "gdn: dtype %d", dtype);
   }
