@@ -223,8 +223,8 @@ def decisions_bench(n_req: int, dev, world: int, dist_mod):
 
 
 def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
-    """cfg4 (Qwen3.5-shaped GDN hybrid, seed 2, 16384-token state, 32
-    questions of U[32,128] tokens) or cfg5 (LFM2-shaped, seed 3, 65536-token
+    """cfg4 (Qwen3.5-shaped GDN hybrid, seed 2, 16384-token state run once
+    as one pass, 32 questions of U[32,128] tokens) or cfg5 (LFM2-shaped, seed 3, 65536-token
     state in 512-token chunks, 64 questions of 64 tokens): the state is
     prefilled once into the cached prefix state, the questions run as
     right-padded rows continuing it (hybrid.rs:697-739).  4 option codes,
@@ -249,7 +249,9 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
         dec = hybrid.Lfm2(cfg, w, torch.bfloat16, dev, max_len=plen + 1024, arena_rows=plen + 8192, split=split)
     del w
     codes = workloads.code_ids(4)
-    eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=512, pass_tokens=8192, prefix_cache_tokens=plen)
+    # cfg4's state is run once: one 16384-token pass; cfg5's is prefilled in 512-token chunks
+    eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=plen if name == "cfg4" else 512, pass_tokens=8192,
+                              prefix_cache_tokens=plen)
     vocab = cfg["vocab_size"] - 1
     stream = 0 if split is not None else rank  # a split model runs the same requests on every rank
     reqs = [workloads.decision_request(20_000 * (stream + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]
