@@ -68,7 +68,14 @@ typedef struct cevk_segment {
   int32_t prefix_len;
   int32_t self_off;
   int32_t tile_start; /* first work tile of the segment; set by cevk_attn_schedule */
+  int32_t flags;      /* CEVK_SEG_* */
 } cevk_segment;
+
+/* Segment flag: every row of the segment sees all q_len of its own rows,
+ * not only the earlier ones (Attn::Bidirectional, decoder.rs:109-116: a
+ * right-padded row's real tokens as one such segment; its padding never
+ * reaches a real token). */
+#define CEVK_SEG_BIDIRECTIONAL 1
 
 /* Validates host-side `segs` against the query/KV row counts (every range
  * inside its buffer; CEVK_E_RANGE otherwise), fills their `tile_start` and
@@ -217,6 +224,25 @@ int cevk_gdn_chunk_prefill_noalloc(const void* conv_out, int32_t C, const void* 
                                    const void* norm_w, float eps, const float* s_in, int64_t s_batch_stride,
                                    float* s_out, void* y, int32_t B, int32_t T, int32_t nk, int32_t nv, int32_t dk,
                                    int32_t dv, int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Served debiased probabilities (run_debiased's answer math,
+ * service.rs:288-348 with math::{softmax, log_softmax}, math.rs:7-18), on
+ * the device so that only k values per question cross to the host.
+ *   logits: [n_variants, ld] f32 code logits of every rotation variant in
+ *     display order (readout rows), cf_logits: the same rows of the
+ *     content-free calibration twin or NULL;
+ *   span: [n_questions + 1] variant ranges of the questions;
+ *   n_options: [n_questions] option counts (<= ld <= 32);
+ *   order: [n_variants, ld] canonical option shown at each display position;
+ *   scores: [n_questions, out_ld] f32, probs: [n_questions, out_ld] f64.
+ * score_o = mean over variants of log_softmax(z)[pos] - log_softmax(cf)[pos]
+ * at the canonical option o shown at pos, rounded to f32; probs =
+ * softmax(score), f64 like the reference.  No counterpart function in the
+ * reference (it runs this on the host). */
+int cevk_debias(const float* logits, const float* cf_logits, int32_t ld, const int32_t* span,
+                const int32_t* n_options, const int32_t* order, int32_t n_questions, float* scores, double* probs,
+                int32_t out_ld, void* stream);
 
 /* ------------------------------------------------------------------------
  * LFM2 gated short convolution (ShortConv::forward, lfm2.rs:199-219):

@@ -105,6 +105,20 @@ def causal_mask(t: int, past: int) -> torch.Tensor:
     return m
 
 
+def bidirectional_mask(t: int, lengths: list[int]) -> torch.Tensor:
+    """(B, T, T) additive mask of ``Attn::Bidirectional`` rows
+    (qwen35.rs:483-498, decoder.rs:109-116): every real token of a row sees
+    every real token of it, padding columns are hidden, and a padding query
+    keeps its own diagonal so its softmax stays finite."""
+    b = len(lengths)
+    m = torch.zeros(b, t, t)
+    for r, n in enumerate(lengths):
+        m[r, :, n:] = NEG_INF
+        for i in range(n, t):
+            m[r, i, i] = 0.0
+    return m
+
+
 def depthwise_conv1d(x: torch.Tensor, kernel: torch.Tensor) -> torch.Tensor:
     """x (B, C, L), kernel (C, 1, K) -> (B, C, L-K+1) as K shifted
     multiply-adds in x's dtype (decoder.rs:137-151)."""

@@ -20,7 +20,10 @@ P, I32, I64, F, D, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_double,
 class Segment(C.Structure):
     """``cevk_segment``."""
     _fields_ = [("q_start", I32), ("q_len", I32), ("prefix_off", I32), ("prefix_len", I32),
-                ("self_off", I32), ("tile_start", I32)]
+                ("self_off", I32), ("tile_start", I32), ("flags", I32)]
+
+
+SEG_BIDIRECTIONAL = 1  # CEVK_SEG_BIDIRECTIONAL
 
 
 # name -> (restype, argtypes), exactly the declarations of include/cevk.h
@@ -33,6 +36,7 @@ SIGNATURES = {
     "cevk_qk_norm_rope": (C.c_int, [P, I32, I32, I32, I32, P, P, F, I32, P, D, I32, P, P, P, I32, P, I32, I32, I32, I32, I32, P]),
     "cevk_rms_norm": (C.c_int, [P, P, P, P, P, I32, I32, F, I32, I32, P]),
     "cevk_swiglu": (C.c_int, [P, P, I32, I32, I32, P]),
+    "cevk_debias": (C.c_int, [P, P, I32, P, P, P, I32, P, P, I32, P]),
     "cevk_embed": (C.c_int, [P, P, P, I32, I32, I32, I32, P]),
     "cevk_sigmoid_gate": (C.c_int, [P, P, I32, I32, P, I32, I32, I32, I32, P]),
     "cevk_readout": (C.c_int, [P, P, I32, P, F, I32, P, I32, P, P, I32, I32, P]),

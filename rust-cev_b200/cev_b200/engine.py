@@ -44,7 +44,8 @@ class Request:
 @dataclass
 class Readout:
     """(backend.rs:16-26) option logits in display order and the final hidden
-    state at the answer position, both f32 on the host."""
+    state at the answer position, both f32 (on the host, or on the device for
+    an engine built with ``device_readout``)."""
     logits: torch.Tensor
     hidden: torch.Tensor
 
@@ -68,12 +69,17 @@ class _Plan:
 
 
 class Engine:
-    def __init__(self, model: Qwen3, code_ids, prefill_chunk=512, pass_tokens=2048, prefix_cache_tokens=65536):
+    def __init__(self, model: Qwen3, code_ids, prefill_chunk=512, pass_tokens=2048, prefix_cache_tokens=65536,
+                 device_readout=False):
+        """``device_readout``: readouts stay on the device (for the on-device
+        debias epilogue); otherwise they are host tensors like the
+        reference's ``BackendOutput``."""
         self.model = model
         self.code_head = model.head_rows(code_ids).contiguous()
         self.prefill_chunk = prefill_chunk
         self.pass_tokens = pass_tokens
         self.cache = PrefixCache(prefix_cache_tokens)
+        self.device_readout = device_readout
 
     # engine.rs:327-363 after tokenisation
     def _plan(self, req: Request) -> _Plan:
@@ -176,7 +182,8 @@ class Engine:
             x = m.run_tokens(tokens, pos, rows, segs)
             g = torch.tensor(gather, dtype=torch.int32).pin_memory().to(m.device, non_blocking=True)
             hid, logits = ops.readout(x, g, m.norm_w, m.eps, False, self.code_head)
-            hid, logits = hid.cpu(), logits.cpu()
+            if not self.device_readout:
+                hid, logits = hid.cpu(), logits.cpu()
         finally:
             m.arena.release(scratch, max(n_scratch, 1))
         for p in plans:

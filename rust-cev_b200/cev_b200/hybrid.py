@@ -275,7 +275,8 @@ class HybridEngine:
     """Codes readout of the hybrid engine (hybrid.rs:155-165, 454-772)."""
 
     def __init__(self, decoder: _HybridDecoder, code_ids, pad_id: int, prefill_chunk=512, pass_tokens=2048,
-                 prefix_cache_tokens=65536):
+                 prefix_cache_tokens=65536, device_readout=False):
+        self.device_readout = device_readout  # readouts stay on the device (on-device debias)
         self.decoder = decoder
         self.head = decoder.head_rows(code_ids).contiguous()
         self.pad_id = pad_id
@@ -338,7 +339,8 @@ class HybridEngine:
                 x, t = self.rows(state, rows)
                 g = torch.tensor([i * t + len(r) - 1 for i, r in enumerate(rows)], dtype=torch.int32)
                 hid, logits = ops.readout(x, g.to(d.device), d.norm_w, d.eps, d.plus_one, self.head)
-                hid, logits = hid.cpu(), logits.cpu()
+                if not self.device_readout:
+                    hid, logits = hid.cpu(), logits.cpu()
                 for i, r in enumerate(rows):
                     k = req.n_options[start + i]
                     readouts.append(Readout(logits[i, :k].clone(), hid[i].clone()))

@@ -14,7 +14,7 @@ import math
 
 import torch
 
-from ._lib import BF16, F32, Segment, check, lib
+from ._lib import BF16, F32, SEG_BIDIRECTIONAL, Segment, check, lib  # noqa: F401 (SEG_BIDIRECTIONAL re-exported)
 
 
 def _dt(*ts) -> int:
@@ -50,7 +50,9 @@ class AttnPlan:
     """Segments of one packed attention call, scheduled and on the device.
 
     ``segs``: iterable of (q_start, q_len, prefix_off, prefix_len, self_off)
-    -- see ``cevk_segment``.  Built once per pass and shared by every layer.
+    or (..., flags) -- see ``cevk_segment``; ``flags`` ``SEG_BIDIRECTIONAL``
+    makes every row see all of its segment's own rows.  Built once per pass
+    and shared by every layer.
     """
 
     def __init__(self, segs, n_tokens: int, n_kv_rows: int, hq: int, hkv: int, head_dim: int, dtype: torch.dtype,
@@ -59,7 +61,8 @@ class AttnPlan:
         n = len(segs)
         arr = (Segment * max(n, 1))()
         for i, s in enumerate(segs):
-            arr[i].q_start, arr[i].q_len, arr[i].prefix_off, arr[i].prefix_len, arr[i].self_off = (int(x) for x in s)
+            arr[i].q_start, arr[i].q_len, arr[i].prefix_off, arr[i].prefix_len, arr[i].self_off = (int(x) for x in s[:5])
+            arr[i].flags = int(s[5]) if len(s) > 5 else 0
         tiles = C.c_int32(0)
         dt = BF16 if dtype == torch.bfloat16 else F32
         check(lib().cevk_attn_schedule(arr, n, n_tokens, n_kv_rows, hq, hkv, head_dim, dt, C.byref(tiles)))
@@ -229,6 +232,19 @@ def short_conv(bcx: torch.Tensor, B: int, T: int, d: int, conv_w: torch.Tensor, 
     check(lib().cevk_short_conv(_p(bcx), _p(conv_w), _p(bias), _p(tail_in), tbs, _p(tail_out), _p(out), B, T, d, K,
                                 _dt(bcx, conv_w), _s()))
     return out
+
+
+def debias(logits: torch.Tensor, cf_logits, span: torch.Tensor, n_options: torch.Tensor, order: torch.Tensor):
+    """Served (scores f32, probabilities f64) per question on the device
+    (service.rs:288-348).  logits / cf_logits [n_variants, ld] f32 (cf may
+    be None), span [n_q + 1], n_options [n_q], order [n_variants, ld] int32."""
+    _cuda(logits, span, n_options, order, cf_logits)
+    n_q, ld = n_options.shape[0], logits.shape[1]
+    scores = torch.empty(n_q, ld, dtype=torch.float32, device=logits.device)
+    probs = torch.empty(n_q, ld, dtype=torch.float64, device=logits.device)
+    check(lib().cevk_debias(_p(logits), _p(cf_logits), ld, _p(span), _p(n_options), _p(order), n_q, _p(scores),
+                            _p(probs), ld, _s()))
+    return scores, probs
 
 
 def device_status() -> None:

@@ -78,10 +78,22 @@ def log_softmax(z) -> list:
     return [v - lse for v in z]
 
 
-def run_debiased(engine, prefix, questions, mode, code_ids, sep_id, cf_prefix=None, max_permutations=4):
-    """Served (scores, probabilities) per question in canonical option order."""
+def run_debiased(engine, prefix, questions, mode, code_ids, sep_id, cf_prefix=None, max_permutations=4,
+                 on_device=False):
+    """Served (scores, probabilities) per question in canonical option order.
+    ``on_device``: the answer math runs on the GPU (``cevk_debias``) over the
+    readouts left on the device, and only the k probabilities and scores per
+    question come back to the host."""
     if mode not in MODES:
         raise ValueError(f"unknown debias mode `{mode}`")
+    if on_device:
+        saved = engine.device_readout
+        engine.device_readout = True
+        try:
+            return _run_debiased_device(engine, prefix, questions, mode, code_ids, sep_id, cf_prefix,
+                                        max_permutations)
+        finally:
+            engine.device_readout = saved
     variants, spans = [], []
     for q in questions:
         start = len(variants)
@@ -111,3 +123,37 @@ def run_debiased(engine, prefix, questions, mode, code_ids, sep_id, cf_prefix=No
         scores.append(score)
         probs.append(softmax(score))
     return scores, probs
+
+
+def _run_debiased_device(engine, prefix, questions, mode, code_ids, sep_id, cf_prefix, max_permutations):
+    import torch
+
+    from . import ops
+    variants, span = [], [0]
+    for q in questions:
+        for s in shifts(mode, len(q.options), max_permutations):
+            variants.append(q if s == 0 else q.rotated(s))
+        span.append(len(variants))
+    suffixes = [v.render(code_ids, sep_id) for v in variants]
+    n_opts = [len(v.options) for v in variants]
+    main = Request(list(prefix), suffixes, n_opts)
+    if mode in ("calibrate", "full"):
+        out, twin = engine.run_many([main, Request(list(cf_prefix), suffixes, n_opts)])
+    else:
+        out, twin = engine.run_many([main])[0], None
+    ld = max(n_opts)
+
+    def rows(readouts):
+        z = [r.logits for r in readouts]
+        if any(t.shape[0] != ld for t in z):
+            z = [torch.nn.functional.pad(t, (0, ld - t.shape[0])) for t in z]
+        return torch.stack(z).float().contiguous()
+
+    dev = out.readouts[0].logits.device
+    order = torch.tensor([list(v.order) + [0] * (ld - len(v.order)) for v in variants], dtype=torch.int32)
+    k_q = torch.tensor([len(q.options) for q in questions], dtype=torch.int32)
+    scores, probs = ops.debias(rows(out.readouts), None if twin is None else rows(twin.readouts),
+                               torch.tensor(span, dtype=torch.int32).to(dev), k_q.to(dev), order.to(dev))
+    scores, probs = scores.cpu(), probs.cpu()
+    ks = k_q.tolist()
+    return ([scores[i, :k].tolist() for i, k in enumerate(ks)], [probs[i, :k].tolist() for i, k in enumerate(ks)])

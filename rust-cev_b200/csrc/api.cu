@@ -79,6 +79,7 @@ int cevk_attn_schedule(cevk_segment* segs, int32_t n_segs, int32_t n_tokens, int
   int64_t tiles = 0;
   for (int i = 0; i < n_segs; ++i) {
     const cevk_segment& g = segs[i];
+    if (g.flags & ~CEVK_SEG_BIDIRECTIONAL) return set_error(CEVK_E_SHAPE, "segment %d: unknown flags 0x%x", i, g.flags);
     if (g.q_len < 0 || g.prefix_len < 0 || g.q_start < 0 || g.prefix_off < 0 || g.self_off < 0)
       return set_error(CEVK_E_RANGE, "segment %d: negative offset or length", i);
     if ((int64_t)g.q_start + g.q_len > n_tokens)

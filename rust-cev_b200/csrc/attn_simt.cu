@@ -1,7 +1,8 @@
 // Packed block-masked attention on CUDA cores for f32 runs (the exact
 // parity path of the reference's f32 pipeline).  One warp per (token, query head);
 // lanes split the head dimension; online softmax over the segment's visible
-// keys (prefix range in full, own rows causally).  Same segment descriptors
+// keys (prefix range in full, own rows causally or -- bidirectional segments
+// -- in full).  Same segment descriptors
 // and the same semantics as attn_tc.cu.
 #include "common.cuh"
 
@@ -48,7 +49,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const T* __restrict__ q,
       m = mn;
     };
     for (int j = 0; j < seg.prefix_len; ++j) visit(seg.prefix_off + j);
-    for (int j = 0; j <= t; ++j) visit(seg.self_off + j);
+    const int own = (seg.flags & CEVK_SEG_BIDIRECTIONAL) ? seg.q_len : t + 1;
+    for (int j = 0; j < own; ++j) visit(seg.self_off + j);
     T* orow = o + (size_t)(seg.q_start + t) * o_rs + (size_t)h * D;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {

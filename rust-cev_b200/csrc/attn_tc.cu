@@ -109,7 +109,9 @@ __device__ __forceinline__ Work decode_work(const AttnParams& p, int w, int BN) 
   k.t0 = (tile - k.seg.tile_start) * p.rows_t;
   k.nt = min(p.rows_t, k.seg.q_len - k.t0);
   k.n_pre = (k.seg.prefix_len + BN - 1) / BN;
-  k.n_blk = k.n_pre + (k.t0 + k.nt + BN - 1) / BN;
+  // own blocks: up to the tile's last row (causal) or all of them (bidirectional)
+  const int own_end = (k.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? k.seg.q_len : k.t0 + k.nt;
+  k.n_blk = k.n_pre + (own_end + BN - 1) / BN;
   return k;
 }
 
@@ -321,7 +323,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       mbar_arrive(b_sfree(t));
       // Key column c is visible if c <= lim: inside the prefix for a prefix
       // block, causal for an own block.  Full blocks skip the mask.
-      const int lim = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN - 1 : tq - (j - wk.n_pre) * BN;
+      const int own_last = (wk.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? wk.seg.q_len - 1 : tq;
+      const int lim = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN - 1 : own_last - (j - wk.n_pre) * BN;
       if (lim < BN - 1) {
 #pragma unroll
         for (int c = 0; c < BN; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
@@ -384,7 +387,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // rows are whatever the buffer holds there (possibly NaN/Inf, and
       // 0 * NaN = NaN in the MMA): zero them before PV reads the stage.
       {
-        const int vcount = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN : (wk.t0 + wk.nt) - (j - wk.n_pre) * BN;
+        const int own_rows = (wk.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? wk.seg.q_len : wk.t0 + wk.nt;
+        const int vcount = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN : own_rows - (j - wk.n_pre) * BN;
         if (vcount < BN) {
           const int vst = j % KSV;
           if (!mbar_wait(b_vfull(t, vst), (j / KSV) & 1, abort_flag)) { ok = false; break; }

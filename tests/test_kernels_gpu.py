@@ -282,6 +282,41 @@ def gdn_oracle(conv_out, ab, z, a_log, dt_bias, norm_w, s0, nk, nv, dk, dv, eps=
     return y.reshape(B, T, nv * dv), s
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("hq,hkv,D", [(16, 8, 128), (4, 1, 64), (8, 2, 256)])
+def test_attention_bidirectional_rows_match_oracle(dtype, hq, hkv, D):
+    """Right-padded rows under ``Attn::Bidirectional`` (qwen35.rs:483-498):
+    each row's real tokens are one CEVK_SEG_BIDIRECTIONAL segment; its pad
+    tokens a causal segment over the real ones (pads never reach a real
+    token).  Real rows are compared with the reference's mask."""
+    from cev_b200 import ops
+    T, lengths = 150, [150, 37, 1, 129]
+    n = T * len(lengths)
+    q, k, v = rand_attn(n, n, hq, hkv, D, dtype, 23)
+    segs = []
+    for r, L in enumerate(lengths):
+        base = r * T
+        segs.append((base, L, 0, 0, base, ops.SEG_BIDIRECTIONAL))
+        if L < T:
+            segs.append((base + L, T - L, base, L, base + L))
+    plan = ops.AttnPlan(segs, n, n, hq, hkv, D, dtype, "cuda")
+    out = ops.attend_packed(q, k, v, plan).float().cpu()
+    mask = ref.bidirectional_mask(T, lengths)
+    md = torch.float32 if dtype == torch.float32 else torch.bfloat16
+    for r, L in enumerate(lengths):
+        sl = slice(r * T, (r + 1) * T)
+        qq, kk, vv = (x[sl].cpu().to(md).transpose(0, 1)[None] for x in (q, k, v))
+        want = ref.attend(qq, kk, vv, mask[r].to(md))[0].transpose(0, 1).float()
+        exact = ref.attend(*(x[sl].cpu().float().transpose(0, 1)[None] for x in (q, k, v)), mask[r])[0]
+        exact = exact.transpose(0, 1)
+        err = (out[sl][:L] - exact[:L]).abs().max().item()
+        if dtype == torch.float32:
+            assert err < F32_TOL, (r, err)
+        else:
+            ref_err = (want[:L] - exact[:L]).abs().max().item()
+            assert err < BF16_TOL and err <= ref_err + 1e-4, (r, err, ref_err)
+
+
 @pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 2e-2), (torch.float32, 1e-4)])
 @pytest.mark.parametrize("B,T,with_state", [(1, 150, True), (3, 64, True), (2, 10, False)])
 @pytest.mark.parametrize("ws_kind", ["full", "core"])

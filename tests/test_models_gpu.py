@@ -117,3 +117,58 @@ def test_cfg1_full_pipeline_f32_served_probabilities():
     _, p_ref = osvc.run_debiased(ref, prefix, to_oracle_q(qs), "full", codes, workloads.SEP_ID, cf)
     worst = max(abs(a - b) for pa, pb in zip(p_gpu, p_ref) for a, b in zip(pa, pb))
     assert worst < 5e-5, worst
+
+
+def test_debias_kernel_matches_host_math():
+    """cevk_debias against the host f64 answer math (service.rs:288-348) on
+    random logits: 5 questions, 1-3 rotation variants, 2-4 options, with and
+    without calibration rows."""
+    from cev_b200 import ops, service
+    g = torch.Generator().manual_seed(5)
+    ks, nvar = [2, 3, 4, 4, 3], [1, 2, 3, 2, 3]
+    ld = 4
+    span, order, rows = [0], [], []
+    for k, nv in zip(ks, nvar):
+        for s in range(nv):
+            order.append([(j + s) % k for j in range(k)] + [0] * (ld - k))
+            rows.append(k)
+        span.append(span[-1] + nv)
+    z = torch.randn(len(order), ld, generator=g) * 3
+    cf = torch.randn(len(order), ld, generator=g)
+    for use_cf in (False, True):
+        sc, pr = ops.debias(z.cuda(), cf.cuda() if use_cf else None, torch.tensor(span, dtype=torch.int32).cuda(),
+                            torch.tensor(ks, dtype=torch.int32).cuda(), torch.tensor(order, dtype=torch.int32).cuda())
+        sc, pr = sc.cpu(), pr.cpu()
+        for qi, k in enumerate(ks):
+            score = [0.0] * k
+            n = float(span[qi + 1] - span[qi])
+            for v in range(span[qi], span[qi + 1]):
+                lp = service.log_softmax(z[v, :k].tolist())
+                base = service.log_softmax(cf[v, :k].tolist()) if use_cf else [0.0] * k
+                for pos in range(k):
+                    score[order[v][pos]] += (lp[pos] - base[pos]) / n
+            score = [service._f32(x) for x in score]
+            want = service.softmax(score)
+            assert sc[qi, :k].tolist() == score
+            assert max(abs(a - b) for a, b in zip(pr[qi, :k].tolist(), want)) < 1e-12
+
+
+def test_served_probabilities_on_device_match_oracle():
+    """run_debiased with the answer math on the device (readouts left on
+    the GPU, only k probabilities per question copied back): |dp| < 5e-5
+    against the oracle in f32."""
+    from cev_b200 import service
+    from cev_b200.engine import Engine
+    from cev_b200.qwen3 import Qwen3
+    cfg = configs.tiny_qwen3()
+    w = weights.init_weights(cfg, 22)
+    codes = workloads.code_ids(3)
+    prefix, qs = workloads.decision_request(6, 100, 4, 30, 30, 3, cfg["vocab_size"])
+    cf = [7, 8, 9, 10, 11]
+    gpu = Engine(Qwen3(cfg, w, torch.float32, "cuda", arena_rows=4096), codes, prefill_chunk=64)
+    ref = oeng.Engine(oq3.Qwen3(cfg, w), codes, prefill_chunk=64)
+    _, p_gpu = service.run_debiased(gpu, prefix, qs, "full", codes, workloads.SEP_ID, cf, on_device=True)
+    _, p_ref = osvc.run_debiased(ref, prefix, to_oracle_q(qs), "full", codes, workloads.SEP_ID, cf)
+    worst = max(abs(a - b) for pa, pb in zip(p_gpu, p_ref) for a, b in zip(pa, pb))
+    assert worst < 5e-5, worst
+    assert not gpu.device_readout

@@ -111,3 +111,13 @@ def test_math_softmax():
     p = softmax([1.0, 2.0, 3.0])
     e = [math.exp(v - 3.0) for v in (1.0, 2.0, 3.0)]
     assert all(abs(a - b / sum(e)) < 1e-15 for a, b in zip(p, e))
+
+
+def test_bidirectional_mask_restates_the_reference():
+    """qwen35.rs:483-498: real tokens see all real tokens; pad columns are
+    hidden; a pad query keeps its diagonal."""
+    from oracle import ops
+    m = ops.bidirectional_mask(4, [2, 0])
+    inf = float("-inf")
+    assert m[0].tolist() == [[0, 0, inf, inf], [0, 0, inf, inf], [0, 0, 0, inf], [0, 0, inf, 0]]
+    assert m[1].tolist() == [[0, inf, inf, inf], [inf, 0, inf, inf], [inf, inf, 0, inf], [inf, inf, inf, 0]]
