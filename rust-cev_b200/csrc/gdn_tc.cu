@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
   float* sSw = sB + C;        // beta e^cum
   float* sEq = sSw + C;       // e^cum
   float* sEk = sEq + C;       // e^(last - cum)
+  float* sX = sEk + C;        // [32][36] products of the block inverse
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int ch = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.nv / p.nk);  // key head shared by nv/nk value heads (qwen35.rs:436-441)
@@ -183,36 +184,51 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
     sB[tid] = beta;
     sG[tid] = g;
   }
-  auto unpack = [](const uint4& u, float* dst) {  // 8 bf16 -> two 16-byte stores
+  auto unpack8 = [](const uint4& u, float* f) {
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
-    reinterpret_cast<float4*>(dst)[0] =
-        make_float4(__bfloat162float(e[0]), __bfloat162float(e[1]), __bfloat162float(e[2]), __bfloat162float(e[3]));
-    reinterpret_cast<float4*>(dst)[1] =
-        make_float4(__bfloat162float(e[4]), __bfloat162float(e[5]), __bfloat162float(e[6]), __bfloat162float(e[7]));
+#pragma unroll
+    for (int x = 0; x < 8; ++x) f[x] = __bfloat162float(e[x]);
   };
+  auto store8 = [](float* dst, const float* f, float sc) {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(f[0] * sc, f[1] * sc, f[2] * sc, f[3] * sc);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(f[4] * sc, f[5] * sc, f[6] * sc, f[7] * sc);
+  };
+  // l2norm of the q and k rows from registers (q also * dk^-1/2): the DK/8
+  // threads of a row are consecutive lanes, reduced with shuffles.
+  const float qscale = rsqrtf((float)DK);
 #pragma unroll
   for (int u = 0; u < NL; ++u) {
     const int i = tid + u * 128, r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
-    unpack(qv[u], sQ + r * KP + c8);
-    unpack(kv[u], sK + r * KP + c8);
+    float fq[8], fk[8];
+    unpack8(qv[u], fq);
+    unpack8(kv[u], fk);
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      sq += fq[x] * fq[x];
+      sk += fk[x] * fk[x];
+    }
+#pragma unroll
+    for (int o = DK / 16; o > 0; o >>= 1) {
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    store8(sQ + r * KP + c8, fq, (1.f / sqrtf(sq + 1e-6f)) * qscale);
+    store8(sK + r * KP + c8, fk, 1.f / sqrtf(sk + 1e-6f));
   }
   __syncthreads();
-  // ---- l2norm rows (warp per row), q * dk^-1/2; cumsum of g ----
-  const float qscale = rsqrtf((float)DK);
-  for (int r = warp; r < 2 * C; r += 4) {
-    float* row = r < C ? sQ + r * KP : sK + (r - C) * KP;
-    float ss = 0.f;
-    for (int d = lane; d < DK; d += 32) ss += row[d] * row[d];
-    ss = warp_sum(ss);
-    const float sc = (1.f / sqrtf(ss + 1e-6f)) * (r < C ? qscale : 1.f);
-    for (int d = lane; d < DK; d += 32) row[d] *= sc;
-  }
-  if (tid == 0) {
-    float acc = 0.f;
-    for (int r = 0; r < C; ++r) {
-      acc += sG[r];
-      sG[r] = acc;
+  // ---- cumsum of g over the chunk: warp 0, two tokens a lane, lane scan ----
+  if (warp == 0) {
+    const float g0 = sG[2 * lane], g1 = sG[2 * lane + 1];
+    float sc = g0 + g1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_up_sync(0xffffffffu, sc, o);
+      if (lane >= o) sc += t;
     }
+    const float before = sc - (g0 + g1);
+    sG[2 * lane] = before + g0;
+    sG[2 * lane + 1] = before + g0 + g1;
   }
   __syncthreads();
   if (tid < C) {
@@ -264,26 +280,6 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
       }
   }
   __syncthreads();
-  // ---- T = (I + A)^-1, column c by forward substitution on a thread pair
-  //      (the two halves of each dot product, combined by a shuffle) ----
-  {
-    const int c = tid >> 1, half = tid & 1;
-    for (int i = 0; i < C; ++i) {
-      float a0 = 0.f, a1 = 0.f;
-      if (i > c) {
-        int j = c + half;
-        for (; j + 2 < i; j += 4) {
-          a0 += sA[i * AP + j] * sT[j * AP + c];
-          a1 += sA[i * AP + j + 2] * sT[(j + 2) * AP + c];
-        }
-        for (; j < i; j += 2) a0 += sA[i * AP + j] * sT[j * AP + c];
-      }
-      float tot = a0 + a1;
-      tot += __shfl_xor_sync(0xffffffffu, tot, 1);
-      if (half == 0) sT[i * AP + c] = i == c ? 1.f : (i > c ? -tot : 0.f);
-      __syncwarp();
-    }
-  }
   // q' = q e^cum, k' = k e^(last - cum)
   {
     float* qp = p.qp + ci * C * DK;
@@ -297,11 +293,72 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
       reinterpret_cast<float4*>(kp)[i] = make_float4(k4.x * ek, k4.y * ek, k4.z * ek, k4.w * ek);
     }
   }
+  // ---- T = (I + A)^-1 by recursive block inversion, the reference's
+  //      scheme (qwen35.rs:266-296): inv(I + [[a, 0], [c, d]]) =
+  //      [[ai, 0], [-di c ai, di]].  16 x 16 leaves by forward substitution
+  //      (warp w: diagonal block w, two lanes per column), then the two
+  //      levels' products on the tensor cores. ----
+  {
+    const int b0 = warp * 16, c = lane >> 1, half = lane & 1;
+    for (int i = 0; i < 16; ++i) {
+      float acc = 0.f;
+      if (i > c)
+        for (int j = c + half; j < i; j += 2) acc += sA[(b0 + i) * AP + b0 + j] * sT[(b0 + j) * AP + b0 + c];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (half == 0) sT[(b0 + i) * AP + b0 + c] = i == c ? 1.f : (i > c ? -acc : 0.f);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // 16 x 16 tile = A (16 x K) * B (K x 16), split TF32, into acc[2][4] (D layout)
+  auto mm16 = [&](const float* A, int lda, const float* B, int ldb, int K, float (*acc)[4]) {
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      const Frag<true> fa = frag_a<true>(A, lda, 0, k0, gid, tig);
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        const Frag<true> fb = frag_b<true>(B, ldb, k0, n * 8, gid, tig);
+        mma<true>(acc[n], fa, fb);
+      }
+    }
+  };
+  auto put16 = [&](float* D, int ldd, const float (*acc)[4], float sgn) {
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      *reinterpret_cast<float2*>(D + gid * ldd + n * 8 + 2 * tig) = make_float2(sgn * acc[n][0], sgn * acc[n][1]);
+      *reinterpret_cast<float2*>(D + (gid + 8) * ldd + n * 8 + 2 * tig) = make_float2(sgn * acc[n][2], sgn * acc[n][3]);
+    }
+  };
+  constexpr int XP = 36;
+  if (warp < 2) {  // level 1: T[b+1, b] = -D_{b+1} (A[b+1, b] D_b), b = 0, 2
+    const int r0 = 16 * (2 * warp + 1), c0 = 16 * (2 * warp);
+    float acc[2][4];
+    mm16(sA + r0 * AP + c0, AP, sT + c0 * AP + c0, AP, 16, acc);
+    put16(sX + warp * 16 * XP, XP, acc, 1.f);
+    __syncwarp();
+    mm16(sT + r0 * AP + r0, AP, sX + warp * 16 * XP, XP, 16, acc);
+    put16(sT + r0 * AP + c0, AP, acc, -1.f);
+  }
+  __syncthreads();
+  {  // level 2: X = A[32:, :32] T[:32, :32], then T[32:, :32] = -T[32:, 32:] X (a quadrant per warp)
+    const int qr = (warp >> 1) * 16, qc = (warp & 1) * 16;
+    float acc[2][4];
+    mm16(sA + (32 + qr) * AP, AP, sT + qc, AP, 32, acc);
+    put16(sX + qr * XP + qc, XP, acc, 1.f);
+    __syncthreads();
+    mm16(sT + (32 + qr) * AP + 32, AP, sX + qc, XP, 32, acc);
+    put16(sT + (32 + qr) * AP + qc, AP, acc, -1.f);
+  }
   __syncthreads();  // T complete; q no longer needed
 #pragma unroll
   for (int u = 0; u < NL; ++u) {
     const int i = tid + u * 128, r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
-    unpack(vv[u], sQ + r * KP + c8);
+    float fv[8];
+    unpack8(vv[u], fv);
+    store8(sQ + r * KP + c8, fv, 1.f);
   }
   __syncthreads();
   // ---- W = T (k beta e^cum), U = T (v beta) (T lower triangular) ----
@@ -364,18 +421,25 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
     const int d = i / VS, c = i % VS;
     sS[d * SP + c] = p.s_in ? p.s_in[b * p.s_bs + ((size_t)h * DK + d) * DV + c0 + c] : 0.f;
   }
+  auto load_wq = [&](size_t cj) {
+    const float* w = p.w + cj * C * DK;
+    const float* q = p.qp + cj * C * DK;
+    for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
+      const int r = (i * 4) / DK, d = (i * 4) % DK;
+      cp_async16(sW + r * KP + d, w + 4 * i);
+      cp_async16(sQp + r * KP + d, q + 4 * i);
+    }
+  };
   for (int ch = 0; ch < p.n_chunks; ++ch) {
     const size_t ci = chunk_index(p, b, ch, h);
-    __syncthreads();  // previous chunk done with sW .. sI; state slice written
+    __syncthreads();  // previous chunk done with sKp, sU, sI; state slice written
     {
-      // every 16-byte copy of the chunk in flight at once
-      const float* w = p.w + ci * C * DK;
-      const float* q = p.qp + ci * C * DK;
+      // every 16-byte copy of the chunk in flight at once (W and q' of all
+      // but the first chunk were prefetched during the previous chunk)
       const float* k = p.kp + ci * C * DK;
+      if (ch == 0) load_wq(ci);
       for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
         const int r = (i * 4) / DK, d = (i * 4) % DK;
-        cp_async16(sW + r * KP + d, w + 4 * i);
-        cp_async16(sQp + r * KP + d, q + 4 * i);
         cp_async16(sKp + r * KP + d, k + 4 * i);
       }
       const float* u = p.u + ci * C * DV + c0;
@@ -418,6 +482,9 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
         sU[i * SP + j] -= vn[n][e];
       }
     __syncthreads();
+    // W and q' are done for this chunk: the next chunk's stream in behind
+    // the intra and state-update phases.
+    if (ch + 1 < p.n_chunks) load_wq(chunk_index(p, b, ch + 1, h));
     // out = q' S + intra v_new (intra lower triangular)
 #pragma unroll 1
     for (int k0 = 0; k0 < r0 + 16; k0 += 8) {
@@ -476,7 +543,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
 
 template <int DK, int DV>
 size_t prep_smem() {
-  return sizeof(float) * (2 * C * (DK + 4) + 2 * C * (C + 4) + 5 * C);
+  return sizeof(float) * (2 * C * (DK + 4) + 2 * C * (C + 4) + 5 * C + 32 * 36);
 }
 template <int DK, int DV>
 size_t scan_smem() {
