@@ -340,7 +340,8 @@ def op_bench(args, dev):
                 "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
                 "config": {"workload": f"B{B} T{T} nk{nk} nv{nv} dk{dk} dv{dv}, chunk 64, state in/out",
                            "flop_per_step": flops, "bytes_per_step": nbytes},
-                "roofline": {"bound": "compute (f32 SIMT)", "achieved": tf, "unit": "TFLOP/s",
+                "roofline": {"bound": "latency (sequential chunk scan, mma.sync split TF32)", "achieved": tf,
+                             "unit": "TFLOP/s",
                              "hbm_gbs": nbytes / (ms / 1e3) / 1e9, "hbm_peak_gbs": peak_hbm, "peak_source": src}}
     elif args.op == "conv":
         # cfg5 gated short conv layer (d 2048, K 3) over a 16384-token run
@@ -362,6 +363,30 @@ def op_bench(args, dev):
                 "config": {"workload": f"B{B} T{T} d{d} K{K} (inputs larger than L2)", "bytes_per_step": nbytes},
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak_hbm, "unit": "GB/s",
                              "frac": gbs / peak_hbm, "peak_source": src + " copy"}}
+    elif args.op == "chunk":
+        # cfg5 attention layer, one 512-token prefill chunk after a 32768-token
+        # cached prefix: all 8 KV heads (one GPU) and one KV head (a rank of
+        # the 8-way KV-head split), planned split-KV against no split
+        P, T, D = 32768, 512, 64
+        line = {"metric": "prefill-chunk attention TFLOP/s (cfg5 layer, 512 tokens after a 32768-token prefix)",
+                "unit": "TFLOP/s", "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
+                "config": {"workload": f"one segment q_len {T}, prefix {P}, head_dim {D}, causal own rows"}}
+        for hq, hkv in ((32, 8), (4, 1)):
+            q = torch.randn(T, hq, D, device=dev, generator=g).bfloat16()
+            k = torch.randn(P + T, hkv, D, device=dev, generator=g).bfloat16()
+            v = torch.randn(P + T, hkv, D, device=dev, generator=g).bfloat16()
+            o = torch.empty_like(q)
+            flops = 4.0 * D * hq * sum(P + i + 1 for i in range(T))
+            res = {}
+            for name, ns in (("split", None), ("unsplit", 1)):
+                plan = ops.AttnPlan([(0, T, 0, P, P)], T, P + T, hq, hkv, D, torch.bfloat16, dev, n_split=ns)
+                ms = timed(lambda: ops.attend_packed(q, k, v, plan, out=o), args.steps, args.warmup, stream)
+                ops.device_status()
+                res[name] = {"tflops": flops / (ms / 1e3) / 1e12, "ms": ms, "n_split": plan.n_split}
+            line[f"hq{hq}_hkv{hkv}"] = res
+        line["value"] = line["hq32_hkv8"]["split"]["tflops"]
+        line["roofline"] = {"bound": "tensor", "achieved": line["value"], "peak": peak_tf, "unit": "TFLOP/s",
+                            "frac": line["value"] / peak_tf, "peak_source": src}
     else:
         raise SystemExit(f"unknown --op {args.op}")
     print(json.dumps(line), flush=True)
@@ -378,8 +403,8 @@ def main():
                     help="also measure cfg3 decisions/sec on this many requests per GPU (0 = skip)")
     ap.add_argument("--hybrid", type=int, default=0,
                     help="also measure cfg4 and cfg5 decisions/sec on this many requests per GPU")
-    ap.add_argument("--op", default="attn", choices=["attn", "gdn", "conv", "cfg3", "cfg4", "cfg5"],
-                    help="attn: the headline line; gdn / conv: one kernel at its layer shape; "
+    ap.add_argument("--op", default="attn", choices=["attn", "gdn", "conv", "chunk", "cfg3", "cfg4", "cfg5"],
+                    help="attn: the headline line; gdn / conv / chunk: one kernel at its layer shape; "
                          "cfg3/4/5: only that config's decisions/sec")
     ap.add_argument("--requests", type=int, default=2, help="requests per GPU for --op cfg3/cfg4/cfg5")
     args = ap.parse_args()
@@ -405,7 +430,7 @@ def main():
         if world > 1:
             dist.barrier()
 
-    if args.op in ("gdn", "conv"):
+    if args.op in ("gdn", "conv", "chunk"):
         if rank == 0:
             op_bench(args, dev)
     elif args.op in ("cfg3", "cfg4", "cfg5"):

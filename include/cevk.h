@@ -99,6 +99,39 @@ int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* 
                              int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
                              int32_t n_segs, int32_t n_tiles, float scale, int32_t dtype, void* stream);
 
+/* Split-KV for calls whose work tiles underfill the GPU (a prefill chunk
+ * after a long cached prefix: few tiles, each walking many key blocks).
+ * The reference has no counterpart (candle runs one matmul per head); it is
+ * a scheduling choice of this library with the same results.
+ *
+ * cevk_attn_split_plan: from the host-side `segs` as filled by
+ * cevk_attn_schedule, returns in *n_split how many CTAs share one tile's
+ * key blocks (1 when the tiles already fill n_sms SMs or the prefixes are
+ * too short to pay) and in *workspace_bytes the workspace that split needs.
+ * bf16 only (f32 plans 1). */
+int cevk_attn_split_plan(const cevk_segment* segs, int32_t n_segs, int32_t n_tiles, int32_t hkv, int32_t head_dim,
+                         int32_t dtype, int32_t n_sms, int32_t* n_split, int64_t* workspace_bytes);
+
+/* Workspace bytes cevk_attn_packed_prefill_split needs for n_split (0 for
+ * n_split <= 1): an f32 partial output row and its log-sum-exp per query
+ * row, head and key range. */
+int64_t cevk_attn_split_workspace_size(int32_t n_tiles, int32_t hkv, int32_t head_dim, int32_t n_split);
+
+/* cevk_attn_packed_prefill with each work tile's key blocks cut into up to
+ * n_split contiguous ranges (each starting inside the segment's prefix; a
+ * tile whose prefix has fewer 64-key blocks than n_split uses that many),
+ * run by separate CTAs that leave normalised f32 partial rows and their
+ * log-sum-exp in `workspace` (16-byte aligned, at least
+ * cevk_attn_split_workspace_size bytes); a second kernel on the same stream
+ * merges them into o.  Tiles with one range write o directly.  n_split 1
+ * (and every f32 call) is cevk_attn_packed_prefill.  The workspace serves
+ * one call at a time. */
+int cevk_attn_packed_prefill_split(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
+                                   int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
+                                   int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
+                                   int32_t n_segs, int32_t n_tiles, float scale, int32_t n_split, void* workspace,
+                                   int64_t workspace_bytes, int32_t dtype, void* stream);
+
 /* ------------------------------------------------------------------------
  * Per-head RMSNorm + (partial) RoPE at explicit positions, writing Q and
  * the arena K/V rows.  Replaces q_norm/k_norm + Rotary::apply + the K/V

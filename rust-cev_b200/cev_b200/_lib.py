@@ -33,6 +33,10 @@ SIGNATURES = {
     "cevk_device_status": (C.c_int, []),
     "cevk_attn_schedule": (C.c_int, [P, I32, I32, I32, I32, I32, I32, I32, P]),
     "cevk_attn_packed_prefill": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32, P]),
+    "cevk_attn_split_plan": (C.c_int, [P, I32, I32, I32, I32, I32, I32, P, P]),
+    "cevk_attn_split_workspace_size": (I64, [I32, I32, I32, I32]),
+    "cevk_attn_packed_prefill_split": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32,
+                                                 P, I64, I32, P]),
     "cevk_qk_norm_rope": (C.c_int, [P, I32, I32, I32, I32, P, P, F, I32, P, D, I32, P, P, P, I32, P, I32, I32, I32, I32, I32, P]),
     "cevk_rms_norm": (C.c_int, [P, P, P, P, P, I32, I32, F, I32, I32, P]),
     "cevk_swiglu": (C.c_int, [P, P, I32, I32, I32, P]),

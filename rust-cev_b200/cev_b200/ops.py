@@ -53,10 +53,15 @@ class AttnPlan:
     or (..., flags) -- see ``cevk_segment``; ``flags`` ``SEG_BIDIRECTIONAL``
     makes every row see all of its segment's own rows.  Built once per pass
     and shared by every layer.
+
+    ``n_split``: key ranges per work tile (split-KV, for calls whose tiles
+    underfill the GPU); None plans it from the SM count
+    (``cevk_attn_split_plan``), 1 disables it.  A split plan owns a device
+    workspace that serves one call at a time.
     """
 
     def __init__(self, segs, n_tokens: int, n_kv_rows: int, hq: int, hkv: int, head_dim: int, dtype: torch.dtype,
-                 device):
+                 device, n_split: int | None = None):
         segs = list(segs)
         n = len(segs)
         arr = (Segment * max(n, 1))()
@@ -74,6 +79,15 @@ class AttnPlan:
         self.n_tiles = tiles.value
         self.n_tokens, self.n_kv_rows = n_tokens, n_kv_rows
         self.hq, self.hkv, self.head_dim = hq, hkv, head_dim
+        if n_split is None:
+            dev = torch.device(device)
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 0
+            ns, nb = C.c_int32(1), C.c_int64(0)
+            check(lib().cevk_attn_split_plan(arr, n, self.n_tiles, hkv, head_dim, dt, sms, C.byref(ns), C.byref(nb)))
+            n_split = ns.value
+        self.n_split = max(1, int(n_split)) if dt == BF16 else 1
+        ws = lib().cevk_attn_split_workspace_size(self.n_tiles, hkv, head_dim, self.n_split)
+        self.workspace = torch.empty(ws, dtype=torch.uint8, device=device) if ws > 0 else None
 
 
 def attend_packed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan: AttnPlan, scale: float | None = None,
@@ -90,8 +104,15 @@ def attend_packed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan: AttnP
     if out is None:
         out = torch.empty(T, hq, D, dtype=q.dtype, device=q.device)
     scale = 1.0 / math.sqrt(D) if scale is None else scale
-    check(lib().cevk_attn_packed_prefill(_p(q), _p(k), _p(v), _p(out), T, S, hq, hkv, D, q.stride(0), k.stride(0),
-                                         out.stride(0), _p(plan.dev), plan.n_segs, plan.n_tiles, scale, dt, _s()))
+    if plan.n_split > 1:
+        ws = plan.workspace
+        check(lib().cevk_attn_packed_prefill_split(_p(q), _p(k), _p(v), _p(out), T, S, hq, hkv, D, q.stride(0),
+                                                   k.stride(0), out.stride(0), _p(plan.dev), plan.n_segs,
+                                                   plan.n_tiles, scale, plan.n_split, _p(ws), ws.numel(), dt, _s()))
+    else:
+        check(lib().cevk_attn_packed_prefill(_p(q), _p(k), _p(v), _p(out), T, S, hq, hkv, D, q.stride(0),
+                                             k.stride(0), out.stride(0), _p(plan.dev), plan.n_segs, plan.n_tiles,
+                                             scale, dt, _s()))
     return out
 
 

@@ -2,6 +2,7 @@
 // validation of shapes and descriptors, and dispatch to the kernels.
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -32,7 +33,7 @@ int check_launch(const char* what) {
 
 int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
                    int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
-                   cudaStream_t stream);
+                   int n_split, void* workspace, cudaStream_t stream);
 int attn_simt_launch(const void* q, const void* k, const void* v, void* o, int hq, int hkv, int D, int q_rs, int kv_rs,
                      int o_rs, const cevk_segment* segs, int n_segs, float scale, cudaStream_t stream);
 
@@ -95,10 +96,36 @@ int cevk_attn_schedule(cevk_segment* segs, int32_t n_segs, int32_t n_tokens, int
   return CEVK_OK;
 }
 
-int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
-                             int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
-                             int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
-                             int32_t n_segs, int32_t n_tiles, float scale, int32_t dtype, void* stream) {
+int64_t cevk_attn_split_workspace_size(int32_t n_tiles, int32_t hkv, int32_t head_dim, int32_t n_split) {
+  if (n_split <= 1 || n_tiles <= 0 || hkv <= 0 || head_dim <= 0) return 0;
+  return (int64_t)n_tiles * hkv * n_split * 128 * (head_dim + 1) * 4;
+}
+
+int cevk_attn_split_plan(const cevk_segment* segs, int32_t n_segs, int32_t n_tiles, int32_t hkv, int32_t head_dim,
+                         int32_t dtype, int32_t n_sms, int32_t* n_split, int64_t* workspace_bytes) {
+  if ((!segs && n_segs > 0) || !n_split || !workspace_bytes) return set_error(CEVK_E_SHAPE, "split plan: null argument");
+  *n_split = 1;
+  *workspace_bytes = 0;
+  if (dtype != CEVK_BF16 || n_segs <= 0 || n_tiles <= 0 || hkv <= 0 || n_sms <= 0) return CEVK_OK;
+  // One wave: two resident CTAs per SM for head_dim <= 128, one for 256.
+  const int64_t slots = (int64_t)n_sms * (head_dim <= 128 ? 2 : 1);
+  const int64_t n_work = (int64_t)n_tiles * hkv;
+  int max_pre = 0;
+  for (int i = 0; i < n_segs; ++i) max_pre = std::max(max_pre, (segs[i].prefix_len + 63) / 64);
+  // Split while the items still fit one wave and every range keeps at
+  // least 8 key blocks (512 keys) to amortise its Q load and epilogue.
+  int64_t s = std::min<int64_t>({slots / n_work, (int64_t)max_pre / 8, 32});
+  if (s < 2 || n_work * s >= (1ll << 30)) return CEVK_OK;
+  *n_split = (int32_t)s;
+  *workspace_bytes = cevk_attn_split_workspace_size(n_tiles, hkv, head_dim, (int32_t)s);
+  return CEVK_OK;
+}
+
+static int packed_prefill(const void* q, const void* k, const void* v, void* o, int32_t n_tokens, int32_t n_kv_rows,
+                          int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride, int32_t kv_row_stride,
+                          int32_t o_row_stride, const cevk_segment* segs_dev, int32_t n_segs, int32_t n_tiles,
+                          float scale, int32_t n_split, void* workspace, int64_t workspace_bytes, int32_t dtype,
+                          void* stream) {
   if (!q || !k || !v || !o || (!segs_dev && n_segs > 0)) return set_error(CEVK_E_SHAPE, "attention: null pointer");
   if (hkv <= 0 || hq % hkv != 0) return set_error(CEVK_E_SHAPE, "hq (%d) must be a multiple of hkv (%d)", hq, hkv);
   if (q_row_stride < hq * head_dim || o_row_stride < hq * head_dim || kv_row_stride < hkv * head_dim)
@@ -111,13 +138,39 @@ int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* 
     if ((q_row_stride % 8) || (kv_row_stride % 8) || (o_row_stride % 8))
       return set_error(CEVK_E_SHAPE, "attention: bf16 row strides must be multiples of 8 elements");
     if (128 % (hq / hkv) != 0) return set_error(CEVK_E_SHAPE, "attention: hq/hkv must divide 128");
+    if (n_split < 1 || (int64_t)n_tiles * hkv * n_split >= (1ll << 30))
+      return set_error(CEVK_E_SHAPE, "attention: split count %d out of range", n_split);
+    if (n_split > 1) {
+      const int64_t need = cevk_attn_split_workspace_size(n_tiles, hkv, head_dim, n_split);
+      if (!workspace || workspace_bytes < need)
+        return set_error(CEVK_E_SHAPE, "attention: split workspace of %lld bytes, %lld needed", (long long)workspace_bytes,
+                         (long long)need);
+      if ((uintptr_t)workspace & 15) return set_error(CEVK_E_SHAPE, "attention: split workspace must be 16-byte aligned");
+    }
     return attn_tc_launch(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
-                          segs_dev, n_segs, n_tiles, scale, st);
+                          segs_dev, n_segs, n_tiles, scale, n_split, workspace, st);
   }
   if (dtype == CEVK_F32)
     return attn_simt_launch(q, k, v, o, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride, segs_dev, n_segs,
                             scale, st);
   return set_error(CEVK_E_UNSUPPORTED, "attention: dtype %d", dtype);
+}
+
+int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
+                             int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
+                             int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
+                             int32_t n_segs, int32_t n_tiles, float scale, int32_t dtype, void* stream) {
+  return packed_prefill(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
+                        segs_dev, n_segs, n_tiles, scale, 1, nullptr, 0, dtype, stream);
+}
+
+int cevk_attn_packed_prefill_split(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
+                                   int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
+                                   int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
+                                   int32_t n_segs, int32_t n_tiles, float scale, int32_t n_split, void* workspace,
+                                   int64_t workspace_bytes, int32_t dtype, void* stream) {
+  return packed_prefill(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
+                        segs_dev, n_segs, n_tiles, scale, n_split, workspace, workspace_bytes, dtype, stream);
 }
 
 }  // extern "C"

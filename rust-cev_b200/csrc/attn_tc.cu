@@ -8,10 +8,10 @@
 // token).  Key tiles of other segments are never loaded, and no mask is
 // materialised: validity is decided per element from the segment descriptor.
 //
-// A CTA runs NT = 2 work tiles (1 for head_dim 256) in ping-pong: one UMMA
-// issuer alternates strictly between the tiles, so while one tile's softmax
-// runs, the tensor cores work on the other tile's QK^T and PV.
-// Warp roles (416 threads for NT = 2):
+// A CTA runs NT work tiles (the launches use NT = 1 with two CTAs per SM
+// for head_dim 64 / 128, so one CTA's softmax overlaps the other's UMMAs;
+// one CTA per SM for head_dim 256).  With NT = 2 one UMMA issuer alternates
+// strictly between the tiles.  Warp roles (256 threads for NT = 1):
 //   warps 0 / 3   TMA producers for Q and K of tile 0 / 1 (one elected lane)
 //   warps 2 / 12  TMA producers for V of tile 0 / 1
 //   warp 1        TMEM allocator + UMMA issuer (one elected lane)
@@ -24,6 +24,14 @@
 // rescale does).  Online softmax in the log2 domain; O is only rescaled when
 // a row max grows by more than 2^8 (values of P stay <= 256, exact in f32
 // accumulation), which keeps TMEM traffic off the common path.
+//
+// Split-KV (n_split > 1): when the call has too few tiles to fill the GPU
+// (a prefill chunk after a long cached prefix), each tile's key blocks are
+// cut into up to n_split contiguous ranges, one CTA each.  Every range
+// starts inside the prefix, whose keys every row of the tile sees, so no
+// row of a range is fully masked.  A ranged CTA writes its normalised f32
+// output rows and their log2-sum-exp to a workspace and attn_combine_kernel
+// merges the ranges; a tile left with one range stores o directly.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -71,10 +79,13 @@ struct AttnParams {
   __nv_bfloat16* o;
   const cevk_segment* segs;
   int n_segs;
-  int n_work;  // work tiles = segment tiles x KV heads
+  int n_work;   // work tiles = segment tiles x KV heads
+  int n_split;  // key ranges per work tile (1: no split); CTA items = n_work * n_split
   int hq, hkv, group, rows_t;
   int o_row_stride;
   float scale_log2;
+  float* part_o;    // [n_work * n_split][128][D] f32 partial outputs (n_split > 1)
+  float* part_lse;  // [n_work * n_split][128] log2-sum-exp of each partial row
 };
 
 __device__ __forceinline__ int find_segment(const cevk_segment* segs, int n, int tile) {
@@ -86,32 +97,50 @@ __device__ __forceinline__ int find_segment(const cevk_segment* segs, int n, int
   return lo;
 }
 
-// One work tile: 128 query rows (G heads x 128/G tokens) of one segment and
-// one KV head, and the key blocks it walks.
+// One CTA item: 128 query rows (G heads x 128/G tokens) of one segment and
+// one KV head, and the key blocks jb .. jb + n_blk - 1 it walks (block
+// numbers count the prefix blocks first, then the segment's own blocks).
 struct Work {
   cevk_segment seg;
-  int kvh, t0, nt, n_pre, n_blk;
+  int kvh, t0, nt, n_pre, n_blk, jb;
+  int item, n_eff;  // CTA item index; key ranges of this tile (1: o stored directly)
   __device__ __forceinline__ int kv_row(int j, int BN) const {
     return j < n_pre ? seg.prefix_off + j * BN : seg.self_off + (j - n_pre) * BN;
   }
 };
 
-__device__ __forceinline__ Work decode_work(const AttnParams& p, int w, int BN) {
+// First block of key range s of n_eff over a tile of `total` blocks whose
+// first n_pre are prefix blocks (n_eff <= n_pre when n_eff > 1): even cuts,
+// pulled back so every range after the first starts inside the prefix.
+__device__ __forceinline__ int range_start(int s, int n_eff, int total, int n_pre) {
+  if (s <= 0) return 0;
+  if (s >= n_eff) return total;
+  return min((int)((long long)s * total / n_eff), n_pre - n_eff + s);
+}
+
+__device__ __forceinline__ Work decode_work(const AttnParams& p, int item, int BN) {
   Work k;
-  if (w >= p.n_work) {
-    k.n_blk = 0;
-    k.nt = 0;
-    return k;
-  }
+  k.n_blk = 0;
+  k.nt = 0;
+  k.jb = 0;
+  k.n_eff = 1;
+  k.item = item;
+  if (item >= p.n_work * p.n_split) return k;
+  const int w = item / p.n_split, sp = item - w * p.n_split;
   const int tile = w / p.hkv;
   k.kvh = w % p.hkv;
   k.seg = p.segs[find_segment(p.segs, p.n_segs, tile)];
   k.t0 = (tile - k.seg.tile_start) * p.rows_t;
-  k.nt = min(p.rows_t, k.seg.q_len - k.t0);
   k.n_pre = (k.seg.prefix_len + BN - 1) / BN;
   // own blocks: up to the tile's last row (causal) or all of them (bidirectional)
-  const int own_end = (k.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? k.seg.q_len : k.t0 + k.nt;
-  k.n_blk = k.n_pre + (own_end + BN - 1) / BN;
+  const int nt = min(p.rows_t, k.seg.q_len - k.t0);
+  const int own_end = (k.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? k.seg.q_len : k.t0 + nt;
+  const int total = k.n_pre + (own_end + BN - 1) / BN;
+  k.n_eff = k.n_pre > 0 ? min(p.n_split, k.n_pre) : 1;
+  if (sp >= k.n_eff) return k;
+  k.nt = nt;
+  k.jb = range_start(sp, k.n_eff, total, k.n_pre);
+  k.n_blk = range_start(sp + 1, k.n_eff, total, k.n_pre) - k.jb;
   return k;
 }
 
@@ -203,7 +232,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         mbar_arrive_expect_tx(b_kfull(t, st), C::KV_BYTES);
 #pragma unroll
         for (int a = 0; a < D / 64; ++a)
-          tma_load_3d(sK(t, st) + a * BN * 128, &tm_k, b_kfull(t, st), a * 64, wk.kvh, wk.kv_row(j, BN));
+          tma_load_3d(sK(t, st) + a * BN * 128, &tm_k, b_kfull(t, st), a * 64, wk.kvh, wk.kv_row(wk.jb + j, BN));
         issued = j + 1;
       }
       // Drain: the Q load and the last load of every stage have landed.
@@ -225,7 +254,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         mbar_arrive_expect_tx(b_vfull(t, st), C::KV_BYTES);
 #pragma unroll
         for (int a = 0; a < D / 64; ++a)
-          tma_load_3d(sV(t, st) + a * BN * 128, &tm_v, b_vfull(t, st), a * 64, wk.kvh, wk.kv_row(j, BN));
+          tma_load_3d(sV(t, st) + a * BN * 128, &tm_v, b_vfull(t, st), a * 64, wk.kvh, wk.kv_row(wk.jb + j, BN));
         issued = j + 1;
       }
       for (int j = max(0, issued - KSV); j < issued; ++j)
@@ -236,7 +265,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     constexpr uint32_t idesc_s = umma_idesc_bf16(128, BN, 0, 0);
     constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 0, 1);
     int nb[NT];
-    bool ok = true;
+    bool ok = true, issued_any = false;
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       nb[t] = decode_work(p, blockIdx.x * NT + t, BN).n_blk;
@@ -255,6 +284,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
       umma_commit(b_sfull(t));
       umma_commit(b_kempty(t, st));
+      issued_any = true;
       return true;
     };
 #pragma unroll
@@ -293,10 +323,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         umma_commit(b_vempty(t, st));
       }
     }
-    // Every UMMA this thread issued has completed before TMEM is freed.
-    umma_commit(b_drain);
-    volatile int never = 0;
-    mbar_wait(b_drain, 0, &never, 1ll << 30);
+    // Every UMMA this thread issued has completed before TMEM is freed
+    // (an item with no key blocks -- a key range past its tile's last --
+    // issued none).
+    if (issued_any) {
+      umma_commit(b_drain);
+      volatile int never = 0;
+      mbar_wait(b_drain, 0, &never, 1ll << 30);
+    }
   } else if (warp >= 4 && warp < 4 + 4 * NT) {
     // ---------------- softmax / correction / epilogue of one tile ----------------
     const int t = (warp - 4) >> 2;
@@ -322,9 +356,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tc_fence_before();
       mbar_arrive(b_sfree(t));
       // Key column c is visible if c <= lim: inside the prefix for a prefix
-      // block, causal for an own block.  Full blocks skip the mask.
+      // block, causal for an own block.  Full blocks skip the mask.  (j
+      // counts this item's blocks; jg is the tile's block number.)
+      const int jg = wk.jb + j;
       const int own_last = (wk.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? wk.seg.q_len - 1 : tq;
-      const int lim = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN - 1 : own_last - (j - wk.n_pre) * BN;
+      const int lim = (jg < wk.n_pre) ? wk.seg.prefix_len - jg * BN - 1 : own_last - (jg - wk.n_pre) * BN;
       if (lim < BN - 1) {
 #pragma unroll
         for (int c = 0; c < BN; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
@@ -388,7 +424,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // 0 * NaN = NaN in the MMA): zero them before PV reads the stage.
       {
         const int own_rows = (wk.seg.flags & CEVK_SEG_BIDIRECTIONAL) ? wk.seg.q_len : wk.t0 + wk.nt;
-        const int vcount = (j < wk.n_pre) ? wk.seg.prefix_len - j * BN : own_rows - (j - wk.n_pre) * BN;
+        const int vcount = (jg < wk.n_pre) ? wk.seg.prefix_len - jg * BN : own_rows - (jg - wk.n_pre) * BN;
         if (vcount < BN) {
           const int vst = j % KSV;
           if (!mbar_wait(b_vfull(t, vst), (j / KSV) & 1, abort_flag)) { ok = false; break; }
@@ -418,12 +454,19 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       const bool store = (tq < wk.seg.q_len) && (r / p.group < wk.nt);
       __nv_bfloat16* orow =
           p.o + (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D;
+      float* prow = p.part_o + ((size_t)wk.item * 128 + r) * D;
+      if (wk.n_eff > 1 && store) p.part_lse[(size_t)wk.item * 128 + r] = m_run + log2f(l_run);
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         float o[32];
         tmem_ld32(tl + C::TM_O + c, o);
         tmem_wait_ld();
-        if (store) {
+        if (store && wk.n_eff > 1) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(prow + c + i) =
+                make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+        } else if (store) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 pv;
@@ -443,6 +486,40 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     tc_fence_after();
     tmem_dealloc(tmem, C::TM_COLS);
   }
+}
+
+// Merges the key ranges of split tiles: o = sum_s 2^(lse_s - m) o_s /
+// sum_s 2^(lse_s - m), m = max_s lse_s, per row; one block of 128 threads
+// per (work tile, group of 1024 / D rows), 8 columns per thread.
+template <int D, int BN>
+__global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
+  const Work wk = decode_work(p, blockIdx.x * p.n_split, BN);
+  if (wk.n_eff <= 1) return;
+  constexpr int CH = D / 8;
+  const int r = blockIdx.y * (128 / CH) + threadIdx.x / CH;
+  const int c = (threadIdx.x % CH) * 8;
+  const int tq = wk.t0 + r / p.group, h = r % p.group;
+  if (!(tq < wk.seg.q_len && r / p.group < wk.nt)) return;
+  const size_t it0 = (size_t)blockIdx.x * p.n_split;
+  float m = -INFINITY;
+  for (int s = 0; s < wk.n_eff; ++s) m = fmaxf(m, p.part_lse[(it0 + s) * 128 + r]);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, wsum = 0.f;
+  for (int s = 0; s < wk.n_eff; ++s) {
+    const float wt = exp2f(p.part_lse[(it0 + s) * 128 + r] - m);
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + ((it0 + s) * 128 + r) * D + c);
+    const float4 a = src[0], b = src[1];
+    wsum += wt;
+    acc[0] += wt * a.x; acc[1] += wt * a.y; acc[2] += wt * a.z; acc[3] += wt * a.w;
+    acc[4] += wt * b.x; acc[5] += wt * b.y; acc[6] += wt * b.z; acc[7] += wt * b.w;
+  }
+  const float inv = 1.f / wsum;
+  uint4 pv;
+  pv.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  pv.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  pv.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+  pv.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4*>(p.o + (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D +
+                            c) = pv;
 }
 
 // ---------------------------------------------------------------------------
@@ -479,7 +556,7 @@ static int make_map(CUtensorMap* m, const void* base, int D, int heads, int rows
 template <int D, int BN, int KSK, int KSV, int NT>
 static int launch_tc(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
                      int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
-                     cudaStream_t stream) {
+                     int n_split, void* workspace, cudaStream_t stream) {
   using C = AttnTc<D, BN, KSK, KSV, NT>;
   const int group = hq / hkv, rows_t = 128 / group;
   CUtensorMap tq, tk, tv;
@@ -499,30 +576,36 @@ static int launch_tc(const void* q, const void* k, const void* v, void* o, int n
   prm.segs = segs;
   prm.n_segs = n_segs;
   prm.n_work = n_tiles * hkv;
+  prm.n_split = n_split;
+  prm.part_o = reinterpret_cast<float*>(workspace);
+  prm.part_lse = prm.part_o + (size_t)prm.n_work * n_split * 128 * D;
   prm.hq = hq;
   prm.hkv = hkv;
   prm.group = group;
   prm.rows_t = rows_t;
   prm.o_row_stride = o_rs;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  const unsigned grid = (unsigned)((prm.n_work + NT - 1) / NT);
+  const unsigned grid = (unsigned)((prm.n_work * n_split + NT - 1) / NT);
   attn_tc_kernel<D, BN, KSK, KSV, NT><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, prm);
-  return check_launch("attn_tc_kernel");
+  const int rc2 = check_launch("attn_tc_kernel");
+  if (rc2 || n_split == 1) return rc2;
+  attn_combine_kernel<D, BN><<<dim3((unsigned)prm.n_work, D / 8), 128, 0, stream>>>(prm);
+  return check_launch("attn_combine_kernel");
 }
 
 int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
                    int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
-                   cudaStream_t stream) {
+                   int n_split, void* workspace, cudaStream_t stream) {
   switch (D) {
     case 64:
       return launch_tc<64, 64, 6, 4, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                     scale, stream);
+                                     scale, n_split, workspace, stream);
     case 128:
       return launch_tc<128, 64, 3, 2, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                      scale, stream);
+                                      scale, n_split, workspace, stream);
     case 256:
       return launch_tc<256, 64, 3, 2, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                      scale, stream);
+                                      scale, n_split, workspace, stream);
     default:
       return set_error(CEVK_E_SHAPE, "bf16 attention supports head_dim 64, 128, 256 (got %d)", D);
   }

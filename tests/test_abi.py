@@ -73,3 +73,32 @@ def test_schedule_rejects_bad_gqa():
     n = C.c_int32()
     assert lib.cevk_attn_schedule(_segs([(0, 1, 0, 0, 0)]), 1, 1, 1, 12, 8, 128, _lib.BF16, C.byref(n)) == _lib.E_SHAPE
     assert lib.cevk_attn_schedule(_segs([(0, 1, 0, 0, 0)]), 1, 1, 1, 24, 8, 128, _lib.BF16, C.byref(n)) == _lib.E_SHAPE
+
+
+def _plan(rows, n_tok, n_kv, hq, hkv, D, sms=148):
+    lib = _lib.lib()
+    arr = _segs(rows)
+    n = C.c_int32()
+    assert lib.cevk_attn_schedule(arr, len(rows), n_tok, n_kv, hq, hkv, D, _lib.BF16, C.byref(n)) == 0
+    ns, nb = C.c_int32(), C.c_int64()
+    assert lib.cevk_attn_split_plan(arr, len(rows), n.value, hkv, D, _lib.BF16, sms, C.byref(ns), C.byref(nb)) == 0
+    return n.value, ns.value, nb.value
+
+
+def test_split_plan_fills_one_wave_of_underfilled_calls():
+    """A 512-token prefill chunk after a long prefix (cfg5's LFM2 chunk:
+    32 Q / 8 KV heads, head_dim 64 -> 16 tiles x 8 KV heads = 128 CTAs on
+    148 SMs x 2) splits in two; one KV head per rank (the 8-way KV-head
+    split) splits 18 ways; a short prefix or an already full call does not
+    split; the workspace is one f32 row + log-sum-exp per range and row."""
+    lib = _lib.lib()
+    tiles, ns, nb = _plan([(0, 512, 0, 32768, 32768)], 512, 33280, 32, 8, 64)
+    assert (tiles, ns) == (16, 2) and nb == 16 * 8 * 2 * 128 * 65 * 4
+    assert nb == lib.cevk_attn_split_workspace_size(tiles, 8, 64, ns)
+    assert _plan([(0, 512, 0, 32768, 32768)], 512, 33280, 4, 1, 64)[1] == 18
+    assert _plan([(0, 512, 0, 448, 448)], 512, 960, 4, 1, 64)[1] == 1        # 7 prefix blocks: too short
+    assert _plan([(0, 512, 0, 4096, 4096)], 512, 4608, 4, 1, 64)[1] == 8     # 64 blocks: ranges of >= 8
+    rows = [(i * 64, 64, 0, 2048, 2048 + i * 64) for i in range(64)]
+    assert _plan(rows, 4096, 6144, 16, 8, 128)[1] == 1                       # 512 CTAs: already full
+    assert _plan([(0, 128, 0, 65536, 65536)], 128, 65664, 16, 4, 256)[1] == 9   # 16 CTAs, one per SM at head_dim 256
+    assert lib.cevk_attn_split_workspace_size(16, 8, 64, 1) == 0

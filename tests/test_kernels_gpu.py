@@ -356,3 +356,61 @@ def test_gdn_conv_matches_oracle(dtype, tol):
     want = ref.silu(ref.depthwise_conv1d(full.float(), w.float())).transpose(1, 2)
     assert close(y.reshape(B, T, C_), want, tol, dtype == torch.bfloat16)
     assert torch.equal(tail_out.cpu(), full[:, :, T:T + K - 1].contiguous())
+
+
+SPLIT_CASES = [
+    # cfg5-shaped prefill chunk (one KV head of the 8-way split), a
+    # bidirectional segment behind a prefix, ragged prefixes, a prefix-less
+    # segment (never split) and head_dim 128 / 256
+    (4, 1, 64, [(0, 512, 0, 3000, 3000)], 512, 3512),
+    (32, 8, 64, [(0, 200, 0, 1111, 1111, 1), (200, 77, 0, 1111, 1311)], 277, 1388),
+    (16, 8, 128, [(0, 64, 0, 2048, 2048), (64, 100, 0, 65, 2112), (164, 40, 0, 0, 2212)], 204, 2252),
+    (16, 4, 256, [(0, 128, 0, 1000, 1000)], 128, 1128),
+    (2, 1, 128, [(0, 37, 0, 100, 300), (37, 150, 0, 100, 337), (187, 5, 100, 0, 487)], 192, 492),
+]
+
+
+@pytest.mark.parametrize("n_split", [None, 2, 3, 7, 32])
+@pytest.mark.parametrize("case", range(len(SPLIT_CASES)))
+def test_attention_split_kv_matches_oracle(case, n_split):
+    """Split-KV (key ranges per tile merged by log-sum-exp) against the
+    reference's attention: ranges of every length, more ranges than prefix
+    blocks, bidirectional and prefix-less segments.  None = the planner's
+    choice for 148 SMs."""
+    from cev_b200 import ops
+    hq, hkv, D, segs, n_tok, n_kv = SPLIT_CASES[case]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 400 + case)
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda", n_split=n_split)
+    if n_split is not None:
+        assert plan.n_split == n_split
+    out = ops.attend_packed(q, k, v, plan)
+    ops.device_status()
+    mask_segs = [s[:5] for s in segs if not (len(s) > 5 and s[5])]
+    check_bf16_attention(out, q, k, v, mask_segs, n_tok)
+    for s in segs:
+        if len(s) > 5 and s[5]:  # bidirectional: own rows in full
+            qs, ql, po, pl, so = s[:5]
+            kk = torch.cat([k[po:po + pl], k[so:so + ql]]).cpu().float().transpose(0, 1)[None]
+            vv = torch.cat([v[po:po + pl], v[so:so + ql]]).cpu().float().transpose(0, 1)[None]
+            want = ref.attend(q[qs:qs + ql].cpu().float().transpose(0, 1)[None], kk, vv, torch.zeros(ql, pl + ql))
+            assert (out[qs:qs + ql].float().cpu() - want[0].transpose(0, 1)).abs().max().item() < BF16_TOL
+
+
+def test_attention_split_kv_ignores_nonfinite_rows():
+    """Split ranges load only visible K/V rows: NaN/Inf elsewhere in the
+    arena leaves the output bits unchanged."""
+    from cev_b200 import ops
+    hq, hkv, D, segs, n_tok, n_kv = SPLIT_CASES[2]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 450)
+    used = torch.zeros(n_kv, dtype=torch.bool)
+    for (qs, ql, po, pl, so) in segs:
+        used[po:po + pl] = True
+        used[so:so + ql] = True
+    k2, v2 = k.clone(), v.clone()
+    k2[~used.cuda()] = float("nan")
+    v2[~used.cuda()] = float("inf")
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda", n_split=5)
+    a = ops.attend_packed(q, k, v, plan)
+    b = ops.attend_packed(q, k2, v2, plan)
+    ops.device_status()
+    assert torch.equal(a, b)
