@@ -366,31 +366,34 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         for (int c = 0; c < BN; ++c) s[c] = (c <= lim) ? s[c] : -INFINITY;
       }
       // Row max of the raw scores (scale > 0 commutes with max): 8
-      // independent chains, then a tree.
+      // independent chains of three-input max, then a tree.
+      static_assert(BN % 16 == 0, "max chains take 16 columns a step");
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = s[i];
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(s[i], s[8 + i]);
 #pragma unroll
-      for (int c = 8; c < BN; c += 8)
+      for (int c = 16; c < BN; c += 16)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], s[c + i]);
-      const float mb = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * p.scale_log2;
+        for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], s[c + i], s[c + 8 + i]);
+      const float mb = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) *
+                       p.scale_log2;
       // Rescale only when the running max grows by more than 2^8.
       const bool need = (j == 0) || (mb > m_run + 8.f);
       const float m_new = need ? mb : m_run;
       const float factor = (j > 0 && need) ? fast_exp2(m_run - m_new) : 1.f;
-      // P = 2^(s*scale - m): one FFMA + one ex2 per element.
-      const float neg = -m_new;
+      // P = 2^(s*scale - m): one packed FFMA per two elements, one ex2
+      // each; the row sum in four packed accumulator pairs.
+      const float neg = -m_new, sl = p.scale_log2;
       float sm8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) sm8[i] = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float e0 = fast_exp2(fmaf(s[c], p.scale_log2, neg));
-        const float e1 = fast_exp2(fmaf(s[c + 1], p.scale_log2, neg));
-        sm8[c & 7] += e0;
-        sm8[(c + 1) & 7] += e1;
+        float x0, x1;
+        ffma2(x0, x1, s[c], s[c + 1], sl, sl, neg, neg);
+        const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+        const int a = (c >> 1) & 3;
+        fadd2(sm8[2 * a], sm8[2 * a + 1], sm8[2 * a], sm8[2 * a + 1], e0, e1);
         pk[c >> 1] = pack_bf16x2(e0, e1);
       }
       const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));

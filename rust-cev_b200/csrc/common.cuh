@@ -62,6 +62,28 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed f32 pairs (sm_100): one instruction computes both lanes of
+// d = a * b + c / d = a + b, each rounded like its scalar form.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+  asm("{\n .reg .b64 pa, pb, pc, pd;\n mov.b64 pa, {%2, %3};\n mov.b64 pb, {%4, %5};\n mov.b64 pc, {%6, %7};\n"
+      " fma.rn.f32x2 pd, pa, pb, pc;\n mov.b64 {%0, %1}, pd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n .reg .b64 pa, pb, pd;\n mov.b64 pa, {%2, %3};\n mov.b64 pb, {%4, %5};\n"
+      " add.rn.f32x2 pd, pa, pb;\n mov.b64 {%0, %1}, pd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// Three-input max (sm_100), NaN handling as fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
