@@ -65,6 +65,26 @@ __device__ __forceinline__ void mma(float* d, const Frag<SPLIT>& a, const Frag<S
     mma_tf32(d, a.lo, b.hi);
   }
 }
+// An m16n8 accumulator whose split products run as three independent
+// chains (hi*hi, hi*lo, lo*hi), summed when read: a third of the dependent
+// MMA latency of accumulating all three into one register set.
+template <bool SPLIT>
+struct Acc {
+  float d[4], c[4], e[4];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = c[i] = e[i] = 0.f;
+  }
+  __device__ __forceinline__ float get(int i) const { return SPLIT ? d[i] + (c[i] + e[i]) : d[i]; }
+};
+template <bool SPLIT>
+__device__ __forceinline__ void mma(Acc<SPLIT>& acc, const Frag<SPLIT>& a, const Frag<SPLIT>& b) {
+  mma_tf32(acc.d, a.hi, b.hi);
+  if (SPLIT) {
+    mma_tf32(acc.c, a.hi, b.lo);
+    mma_tf32(acc.e, a.lo, b.hi);
+  }
+}
 // A fragment of a row-major matrix M (pitch ld) at (r0, k0), optionally with
 // a per-column scale.
 template <bool SPLIT>
@@ -406,12 +426,14 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
   constexpr int KP = DK + 4, SP = VS + 8, AP = C + 4;
   static_assert(DK % 16 == 0 && DK / 16 <= SCAN_THREADS / 32, "16 state rows per warp");
   extern __shared__ float sm[];
-  float* sS = sm;               // [DK][SP]   state slice
-  float* sW = sS + DK * SP;     // [C][KP]
-  float* sQp = sW + C * KP;     // [C][KP]
-  float* sKp = sQp + C * KP;    // [C][KP]
-  float* sU = sKp + C * KP;     // [C][SP]    U slice, then v_new
-  float* sI = sU + C * SP;      // [C][AP]
+  // k', U and intra are double-buffered: chunk ch + 1's copies stream in
+  // while chunk ch computes (W and q' follow once W S and q' S are done).
+  float* sS = sm;                   // [DK][SP]   state slice
+  float* sW = sS + DK * SP;         // [C][KP]
+  float* sQp = sW + C * KP;         // [C][KP]
+  float* sKp0 = sQp + C * KP;       // 2 x [C][KP]
+  float* sU0 = sKp0 + 2 * C * KP;   // 2 x [C][SP]  U slice, then v_new
+  float* sI0 = sU0 + 2 * C * SP;    // 2 x [C][AP]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int sl = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int c0 = sl * VS;
@@ -430,37 +452,49 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
       cp_async16(sQp + r * KP + d, q + 4 * i);
     }
   };
+  auto load_rest = [&](size_t cj, int buf) {
+    const float* k = p.kp + cj * C * DK;
+    float* dk_ = sKp0 + buf * C * KP;
+    for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
+      const int r = (i * 4) / DK, d = (i * 4) % DK;
+      cp_async16(dk_ + r * KP + d, k + 4 * i);
+    }
+    const float* u = p.u + cj * C * DV + c0;
+    float* du = sU0 + buf * C * SP;
+    for (int i = tid; i < C * VS / 4; i += SCAN_THREADS) {
+      const int r = (i * 4) / VS, c = (i * 4) % VS;
+      cp_async16(du + r * SP + c, u + r * DV + c);
+    }
+    const float* in = p.intra + cj * C * C;
+    float* di = sI0 + buf * C * AP;
+    for (int i = tid; i < C * C / 4; i += SCAN_THREADS) {
+      const int r = (i * 4) / C, c = (i * 4) % C;
+      cp_async16(di + r * AP + c, in + 4 * i);
+    }
+  };
+  if (p.n_chunks > 0) {
+    load_wq(chunk_index(p, b, 0, h));
+    load_rest(chunk_index(p, b, 0, h), 0);
+  }
   for (int ch = 0; ch < p.n_chunks; ++ch) {
     const size_t ci = chunk_index(p, b, ch, h);
-    __syncthreads();  // previous chunk done with sKp, sU, sI; state slice written
-    {
-      // every 16-byte copy of the chunk in flight at once (W and q' of all
-      // but the first chunk were prefetched during the previous chunk)
-      const float* k = p.kp + ci * C * DK;
-      if (ch == 0) load_wq(ci);
-      for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
-        const int r = (i * 4) / DK, d = (i * 4) % DK;
-        cp_async16(sKp + r * KP + d, k + 4 * i);
-      }
-      const float* u = p.u + ci * C * DV + c0;
-      for (int i = tid; i < C * VS / 4; i += SCAN_THREADS) {
-        const int r = (i * 4) / VS, c = (i * 4) % VS;
-        cp_async16(sU + r * SP + c, u + r * DV + c);
-      }
-      const float* in = p.intra + ci * C * C;
-      for (int i = tid; i < C * C / 4; i += SCAN_THREADS) {
-        const int r = (i * 4) / C, c = (i * 4) % C;
-        cp_async16(sI + r * AP + c, in + 4 * i);
-      }
-      cp_async_wait_all();
-    }
-    const float el = p.elast[ci];
+    const int buf = ch & 1;
+    float* sKp = sKp0 + buf * C * KP;
+    float* sU = sU0 + buf * C * SP;
+    float* sI = sI0 + buf * C * AP;
+    // This chunk's copies (issued during the previous chunk) have landed,
+    // the previous chunk is done with the other buffers and the state slice
+    // is written.
+    cp_async_wait_all();
     __syncthreads();
-    float vn[2][4], o[2][4];
+    if (ch + 1 < p.n_chunks) load_rest(chunk_index(p, b, ch + 1, h), buf ^ 1);
+    const float el = p.elast[ci];
+    Acc<true> vn[2], o[2];
 #pragma unroll
-    for (int n = 0; n < 2; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) vn[n][e] = o[n][e] = 0.f;
+    for (int n = 0; n < 2; ++n) {
+      vn[n].zero();
+      o[n].zero();
+    }
     // W S and q' S over dk
 #pragma unroll 2
     for (int k0 = 0; k0 < DK; k0 += 8) {
@@ -479,7 +513,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = r0 + gid + (e >> 1) * 8, j = n0 + n * 8 + 2 * tig + (e & 1);
-        sU[i * SP + j] -= vn[n][e];
+        sU[i * SP + j] -= vn[n].get(e);
       }
     __syncthreads();
     // W and q' are done for this chunk: the next chunk's stream in behind
@@ -502,19 +536,21 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
         const int t = ch * C + r0 + gid + hlf * 8;
         if (t < p.T)
           *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n0 + n * 8 + 2 * tig) =
-              make_float2(o[n][2 * hlf], o[n][2 * hlf + 1]);
+              make_float2(o[n].get(2 * hlf), o[n].get(2 * hlf + 1));
       }
     // S = e^last S + k'^T v_new: warp w owns state rows 16 w .. 16 w + 15
     if (warp < DK / 16) {
       const int d0 = warp * 16;
-      float acc[4][4];
+      Acc<true> acc[4];
 #pragma unroll
-      for (int n = 0; n < 4; ++n)
+      for (int n = 0; n < 4; ++n) {
+        acc[n].zero();
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
-          acc[n][e] = sS[d * SP + c] * el;
+          acc[n].d[e] = sS[d * SP + c] * el;
         }
+      }
 #pragma unroll 2
       for (int k0 = 0; k0 < C; k0 += 8) {
         const Frag<true> fk = frag_at<true>(sKp, KP, d0, k0, gid, tig);
@@ -529,7 +565,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
-          sS[d * SP + c] = acc[n][e];
+          sS[d * SP + c] = acc[n].get(e);
         }
     }
   }
@@ -547,7 +583,7 @@ size_t prep_smem() {
 }
 template <int DK, int DV>
 size_t scan_smem() {
-  return sizeof(float) * (DK * (VS + 8) + 3 * C * (DK + 4) + C * (VS + 8) + C * (C + 4));
+  return sizeof(float) * (DK * (VS + 8) + 4 * C * (DK + 4) + 2 * C * (VS + 8) + 2 * C * (C + 4));
 }
 
 template <int DK, int DV>
