@@ -6,7 +6,12 @@ prompt text and the code-vocabulary probe stay with the caller):
 
 * a request's prefix is looked up in the prefix cache; otherwise every
   prefill chunk but the last runs now (engine.rs:249-256) and the last
-  chunk (the "tail") rides in the first packed pass with the questions;
+  chunk (the "tail") rides in the first packed pass with the questions.
+  The reference prefills each request's head on its own; here chunk c of
+  every uncached head of one ``run_many`` call shares a pass (one segment
+  per request, at most ``pass_tokens`` tokens), which gives the projection
+  GEMMs several chunks' rows at once -- the requests are independent, so
+  each one's K/V and readouts are what it computes alone;
 * questions are packed greedily under ``pass_tokens`` (engine.rs:259-287);
 * each pass computes its new tokens' K/V straight into arena rows -- tails
   into their prefix's range, question suffixes into scratch rows -- and
@@ -110,15 +115,17 @@ class Engine:
         try:
             for r in reqs:
                 plans.append(self._plan(r))
+            heads = []
             for p in plans:
                 if not p.cached:
                     tail = min(len(p.prefix), max(self.prefill_chunk, 1))
                     head = len(p.prefix) - tail
                     if head > 0:
-                        self.model.prefill_into(p.kv, p.prefix[:head], 0, self.prefill_chunk)
+                        heads.append((p, p.prefix[:head]))
                     p.head = head
                     p.kv.len = head
                     p.tail = range(head, len(p.prefix))
+            self._prefill_heads(heads)
             items = [(pi, qi) for pi, p in enumerate(plans) for qi in range(len(p.suffixes))]
             readouts = [[None] * len(p.suffixes) for p in plans]
             rest = items
@@ -144,6 +151,31 @@ class Engine:
             for p in plans:
                 if self.cache.peek(p.prefix) is not p.kv and not p.kv.pins:
                     p.kv.release()
+
+    def _prefill_heads(self, heads):
+        """Causal chunked prefill of every (plan, head ids) in ``heads``
+        (qwen3.rs:347-362 per request): chunk c of all heads in one pass of
+        at most ``max(pass_tokens, prefill_chunk)`` tokens, one segment per
+        head seeing its own earlier chunks fully and itself causally."""
+        chunk = max(self.prefill_chunk, 1)
+        cap = max(self.pass_tokens, chunk)
+        n_chunks = max(((len(h) + chunk - 1) // chunk for _, h in heads), default=0)
+        for c in range(n_chunks):
+            tokens, pos, rows, segs = [], [], [], []
+            for p, head in heads:
+                part = head[c * chunk:(c + 1) * chunk]
+                if not part:
+                    continue
+                if tokens and len(tokens) + len(part) > cap:
+                    self.model.run_tokens(tokens, pos, rows, segs)
+                    tokens, pos, rows, segs = [], [], [], []
+                past, n, base = c * chunk, len(part), p.kv.start
+                segs.append((len(tokens), n, base, past, base + past))
+                tokens.extend(part)
+                pos.extend(range(past, past + n))
+                rows.extend(range(base + past, base + past + n))
+            if tokens:
+                self.model.run_tokens(tokens, pos, rows, segs)
 
     @staticmethod
     def pass_layout(plans, batch, scratch_start):

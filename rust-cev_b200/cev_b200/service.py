@@ -109,6 +109,45 @@ def run_debiased(engine, prefix, questions, mode, code_ids, sep_id, cf_prefix=No
         cf = [r.logits for r in twin.readouts]
     else:
         out = engine.run_many([main])[0]
+    return _answers(variants, spans, out, cf)
+
+
+def run_debiased_many(engine, items, mode, code_ids, sep_id, cf_prefix=None, max_permutations=4):
+    """``run_debiased`` over several independent requests ``items`` =
+    [(prefix, questions), ...] in one ``Engine.run_many`` call: their
+    prefill heads share passes chunk by chunk and their questions share
+    packed passes.  Returns one (scores, probabilities) per item, each what
+    ``run_debiased`` returns for that item alone."""
+    if mode not in MODES:
+        raise ValueError(f"unknown debias mode `{mode}`")
+    calib = mode in ("calibrate", "full")
+    per_item, reqs = [], []
+    for prefix, questions in items:
+        variants, spans = [], []
+        for q in questions:
+            start = len(variants)
+            for s in shifts(mode, len(q.options), max_permutations):
+                variants.append(q if s == 0 else q.rotated(s))
+            spans.append(range(start, len(variants)))
+        suffixes = [v.render(code_ids, sep_id) for v in variants]
+        n_opts = [len(v.options) for v in variants]
+        per_item.append((variants, spans))
+        reqs.append(Request(list(prefix), suffixes, n_opts))
+        if calib:
+            reqs.append(Request(list(cf_prefix), suffixes, n_opts))
+    outs = engine.run_many(reqs)
+    results = []
+    for i, (variants, spans) in enumerate(per_item):
+        out = outs[2 * i] if calib else outs[i]
+        cf = [r.logits for r in outs[2 * i + 1].readouts] if calib else [None] * len(variants)
+        results.append(_answers(variants, spans, out, cf))
+    return results
+
+
+def _answers(variants, spans, out, cf):
+    """service.rs:330-346: per question the mean over its variants of
+    log_softmax(z) (minus the calibration log_softmax) at each display
+    position, accumulated at the option shown there; f32 score, softmax."""
     scores, probs = [], []
     for span in spans:
         k = len(variants[span.start].options)

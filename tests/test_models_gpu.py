@@ -172,3 +172,35 @@ def test_served_probabilities_on_device_match_oracle():
     worst = max(abs(a - b) for pa, pb in zip(p_gpu, p_ref) for a, b in zip(pa, pb))
     assert worst < 5e-5, worst
     assert not gpu.device_readout
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 5e-5), (torch.bfloat16, 1e-3)])
+def test_run_many_batched_prefill_matches_one_request_at_a_time(dtype, tol):
+    """Several independent requests in one run_many (their prefill heads
+    share passes chunk by chunk: heads of 5, 2 and 0 chunks, one prefix
+    cached from an earlier call) serve the probabilities each request gets
+    alone, and the oracle's."""
+    from cev_b200 import service
+    from cev_b200.engine import Engine
+    from cev_b200.qwen3 import Qwen3
+    cfg = configs.tiny_qwen3()
+    w = weights.init_weights(cfg, 23)
+    codes = workloads.code_ids(4)
+    items = [workloads.decision_request(40 + i, n, 3, 20, 30, 4, cfg["vocab_size"])
+             for i, n in enumerate([300, 130, 40, 210])]
+
+    def engine():
+        return Engine(Qwen3(cfg, w, dtype, "cuda", arena_rows=8192), codes, prefill_chunk=48, pass_tokens=400)
+
+    alone = engine()
+    want = [service.run_debiased(alone, p, q, "permute", codes, workloads.SEP_ID, max_permutations=2)
+            for p, q in items]
+    batched = engine()
+    service.run_debiased(batched, *items[3], "permute", codes, workloads.SEP_ID, max_permutations=2)  # cache item 3
+    got = service.run_debiased_many(batched, items, "permute", codes, workloads.SEP_ID, max_permutations=2)
+    ref = oeng.Engine(oq3.Qwen3(cfg, w), codes, prefill_chunk=48, pass_tokens=400)
+    for (p, q), (_, pa), (_, pb) in zip(items, want, got):
+        _, po = osvc.run_debiased(ref, p, to_oracle_q(q), "permute", codes, workloads.SEP_ID, max_permutations=2)
+        for x, y, z in zip(pa, pb, po):
+            assert max(abs(u - v) for u, v in zip(x, y)) < tol
+            assert max(abs(u - v) for u, v in zip(y, z)) < tol
