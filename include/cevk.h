@@ -44,6 +44,13 @@ int cevk_version(void);
 /* Reads and clears the device-side error flag raised by bounded waits;
  * synchronises the device.  CEVK_OK or CEVK_E_TIMEOUT. */
 int cevk_device_status(void);
+/* Failure-detection self-test: launches one thread that waits, through the
+ * same bounded wait as the kernels, on a barrier nothing arrives on.  The
+ * wait gives up after limit_cycles (1 .. 2^32) SM clock cycles and raises
+ * the device error record; the kernel then returns normally, so the next
+ * cevk_device_status() returns CEVK_E_TIMEOUT with the record's location
+ * and the context stays usable.  No fault, trap or hang is involved. */
+int cevk_selftest_wait_timeout(int64_t limit_cycles, void* stream);
 
 /* ------------------------------------------------------------------------
  * Packed block-masked prefill attention.

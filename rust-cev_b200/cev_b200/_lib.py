@@ -31,6 +31,7 @@ SIGNATURES = {
     "cevk_last_error": (C.c_char_p, []),
     "cevk_version": (C.c_int, []),
     "cevk_device_status": (C.c_int, []),
+    "cevk_selftest_wait_timeout": (C.c_int, [I64, P]),
     "cevk_attn_schedule": (C.c_int, [P, I32, I32, I32, I32, I32, I32, I32, P]),
     "cevk_attn_packed_prefill": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32, P]),
     "cevk_attn_split_plan": (C.c_int, [P, I32, I32, I32, I32, I32, I32, P, P]),

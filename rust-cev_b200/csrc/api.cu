@@ -37,6 +37,21 @@ int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_t
 int attn_simt_launch(const void* q, const void* k, const void* v, void* o, int hq, int hkv, int D, int q_rs, int kv_rs,
                      int o_rs, const cevk_segment* segs, int n_segs, float scale, cudaStream_t stream);
 
+// One thread waits, through the library's bounded wait, on an mbarrier that
+// nothing arrives on: the wait gives up after `limit` clock cycles, raises the
+// device error record and the kernel returns normally.
+__global__ void wait_timeout_probe_kernel(long long limit) {
+  __shared__ __align__(8) unsigned long long bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    const uint32_t b = smem_u32(&bar);
+    mbar_init(b, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+    mbar_wait(b, 0, &abort_flag, limit);
+  }
+}
+
 }  // namespace cevk
 
 using namespace cevk;
@@ -65,6 +80,12 @@ int cevk_device_status(void) {
                      r.flag, r.info[0], r.info[1], r.info[2], r.info[3], extra);
   }
   return CEVK_OK;
+}
+
+int cevk_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > (1ll << 32)) return set_error(CEVK_E_SHAPE, "selftest: limit out of range");
+  wait_timeout_probe_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_cycles);
+  return check_launch("wait_timeout_probe_kernel");
 }
 
 int cevk_attn_schedule(cevk_segment* segs, int32_t n_segs, int32_t n_tokens, int32_t n_kv_rows, int32_t hq,

@@ -414,3 +414,23 @@ def test_attention_split_kv_ignores_nonfinite_rows():
     b = ops.attend_packed(q, k2, v2, plan)
     ops.device_status()
     assert torch.equal(a, b)
+
+
+def test_bounded_wait_gives_up_reports_and_leaves_the_context_usable():
+    """Failure detection without a fault: a wait on a barrier nothing
+    arrives on gives up after ~4M cycles, cevk_device_status reports
+    CEVK_E_TIMEOUT with the record, the flag clears, and the next kernels
+    run and match the oracle."""
+    from cev_b200 import _lib, ops
+    lib = _lib.lib()
+    assert lib.cevk_device_status() == _lib.OK
+    assert lib.cevk_selftest_wait_timeout(1 << 22, None) == _lib.OK
+    assert lib.cevk_device_status() == _lib.E_TIMEOUT
+    assert "bounded device wait gave up" in lib.cevk_last_error().decode()
+    assert lib.cevk_device_status() == _lib.OK
+    hq, hkv, D, segs, n_tok, n_kv = CASES[2]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 500)
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda")
+    out = ops.attend_packed(q, k, v, plan)
+    ops.device_status()
+    check_bf16_attention(out, q, k, v, segs, n_tok)
