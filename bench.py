@@ -246,6 +246,10 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
         from cev_b200.tp import KvHeadSplit
         split = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"],
                             cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"], rank, world)
+        if os.environ.get("CEV_HEAD_GATHER", "fused") == "fused":
+            # head outputs gathered by the attention epilogue over NVLink
+            # (largest call: 64 right-padded rows x 64 tokens)
+            split.enable_fused_gather(8192, dev)
     w = weights.init_weights(cfg, seed, torch.bfloat16, dev)
     if name == "cfg4":
         dec = hybrid.Qwen35(cfg, w, torch.bfloat16, dev, max_len=plen + 1024, arena_rows=plen + 8192)
@@ -277,9 +281,14 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     if world > 1:
         dist_mod.all_reduce(dt, op=dist_mod.ReduceOp.MAX)
     streams = 1 if split is not None else world
+    gather = None
+    if split is not None:
+        gather = "fused into the attention epilogue (NVLink peer stores)" if split.fused else "NCCL all-gather"
+        if split.fused is not None:
+            split.fused.close()
     return {"value": nq * n_req * streams / dt.item(), "unit": "decisions/s", "requests_per_stream": n_req,
             "seconds": dt.item(), "workload": f"{name}: {plen}-token state, {nq} questions, rows continuing the state",
-            "parallelism": f"kv-head split x{world}" if split is not None else f"dp{world}"}
+            "parallelism": f"kv-head split x{world}" if split is not None else f"dp{world}", "head_gather": gather}
 
 
 def timed(fn, steps, warmup, stream):

@@ -140,6 +140,45 @@ int cevk_attn_packed_prefill_split(const void* q, const void* k, const void* v, 
                                    int64_t workspace_bytes, int32_t dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Head all-gather fused into the attention epilogue, over NVLink peer
+ * memory.  Replaces the NCCL all-gather of the per-head outputs under the
+ * KV-head split of long-prefix attention (lfm2.rs:145-171 per rank, then
+ * out_proj on the gathered [T, Hq * D] rows).
+ *
+ * Setup, once per rank: cevk_ipc_alloc the gathered buffers and an int32
+ * flag array of `world` entries (zeroed), export each with cevk_ipc_handle,
+ * exchange the handles between the ranks (any host channel), cevk_ipc_open
+ * the peers' (peer access is enabled lazily; no multicast objects).
+ * Per call (epoch = 1, 2, ... the same on every rank):
+ *   cevk_attn_packed_prefill_gather  -- this rank's heads, every output row
+ *       stored to each of o_bufs (every rank's gathered buffer, offset to
+ *       this rank's head columns; o_row_stride = the gathered row width);
+ *   cevk_gather_signal  -- after it on the same stream: flag[rank] = epoch
+ *       in every rank's flag array (system-scope release);
+ *   cevk_gather_wait    -- then: until every entry of this rank's flag
+ *       array reaches epoch (bounded by limit_cycles; a timeout raises the
+ *       device error record that cevk_device_status reports).
+ * A rank reuses a gathered buffer for epoch e + 2 at the earliest, so two
+ * buffers alternating by epoch parity never overwrite rows a peer still
+ * reads.
+ * ---------------------------------------------------------------------- */
+#define CEVK_IPC_HANDLE_BYTES 64
+int cevk_ipc_alloc(int64_t bytes, void** dev_ptr);
+int cevk_ipc_free(void* dev_ptr);
+int cevk_ipc_handle(const void* dev_ptr, void* handle);
+int cevk_ipc_open(const void* handle, void** dev_ptr);
+int cevk_ipc_close(void* dev_ptr);
+/* bf16 only; arguments as cevk_attn_packed_prefill_split plus the 1..8
+ * output buffers (16-byte aligned). */
+int cevk_attn_packed_prefill_gather(const void* q, const void* k, const void* v, void* const* o_bufs, int32_t n_bufs,
+                                    int32_t n_tokens, int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim,
+                                    int32_t q_row_stride, int32_t kv_row_stride, int32_t o_row_stride,
+                                    const cevk_segment* segs_dev, int32_t n_segs, int32_t n_tiles, float scale,
+                                    int32_t n_split, void* workspace, int64_t workspace_bytes, void* stream);
+int cevk_gather_signal(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch, void* stream);
+int cevk_gather_wait(const int32_t* flags, int32_t world, int32_t epoch, int64_t limit_cycles, void* stream);
+
+/* ------------------------------------------------------------------------
  * Per-head RMSNorm + (partial) RoPE at explicit positions, writing Q and
  * the arena K/V rows.  Replaces q_norm/k_norm + Rotary::apply + the K/V
  * `cat` (qwen3.rs:190-200; qwen35.rs:529-541 incl. the zero-centred `1+w`

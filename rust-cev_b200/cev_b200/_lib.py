@@ -35,6 +35,15 @@ SIGNATURES = {
     "cevk_attn_schedule": (C.c_int, [P, I32, I32, I32, I32, I32, I32, I32, P]),
     "cevk_attn_packed_prefill": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32, P]),
     "cevk_attn_split_plan": (C.c_int, [P, I32, I32, I32, I32, I32, I32, P, P]),
+    "cevk_ipc_alloc": (C.c_int, [I64, P]),
+    "cevk_ipc_free": (C.c_int, [P]),
+    "cevk_ipc_handle": (C.c_int, [P, P]),
+    "cevk_ipc_open": (C.c_int, [P, P]),
+    "cevk_ipc_close": (C.c_int, [P]),
+    "cevk_attn_packed_prefill_gather": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32,
+                                                  F, I32, P, I64, P]),
+    "cevk_gather_signal": (C.c_int, [P, I32, I32, I32, P]),
+    "cevk_gather_wait": (C.c_int, [P, I32, I32, I64, P]),
     "cevk_attn_split_workspace_size": (I64, [I32, I32, I32, I32]),
     "cevk_attn_packed_prefill_split": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32,
                                                  P, I64, I32, P]),

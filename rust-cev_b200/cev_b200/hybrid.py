@@ -127,7 +127,7 @@ class _HybridDecoder:
             state.next_pos = max(pos) + 1
         return x
 
-    def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot):
+    def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot, attend=None):
         T = h.shape[0]
         hq, hkv, D = self.hq_a, self.hkv_a, self.D
         qkv = F.linear(h, L["qkv"])
@@ -135,7 +135,7 @@ class _HybridDecoder:
         j = self.arena_index[i]
         ops.qk_norm_rope(qkv, q_cols, k_col, v_col, hq, hkv, D, L["qn"], L["kn"], self.eps, self.plus_one, pos_t,
                          self.theta, rot, q, self.arena.k[j], self.arena.v[j], rows_t)
-        return qkv, ops.attend_packed(q, self.arena.k[j], self.arena.v[j], plan)
+        return qkv, (attend or ops.attend_packed)(q, self.arena.k[j], self.arena.v[j], plan)
 
 
 class Qwen35(_HybridDecoder):
@@ -253,7 +253,11 @@ class Lfm2(_HybridDecoder):
         """lfm2.rs:145-171; with a KV-head split, this rank's heads and one
         all-gather of the head outputs before the output projection."""
         hq, hkv, D = self.hq_a, self.hkv_a, self.D
-        _, ctx = self._attn_common(i, L, h, pos_t, rows_t, plan, (0, D), hq * D, (hq + hkv) * D, D)
+        fused = self.split.fused if self.split is not None else None
+        _, ctx = self._attn_common(i, L, h, pos_t, rows_t, plan, (0, D), hq * D, (hq + hkv) * D, D,
+                                   attend=None if fused is None else fused.attend)
+        if fused is not None:  # already gathered by the attention epilogue
+            return F.linear(ctx, L["o"])
         ctx = ctx.view(h.shape[0], hq * D)
         if self.split is not None:
             ctx = self.split.gather(ctx)

@@ -26,6 +26,13 @@ class KvHeadSplit:
         self.rank, self.world, self.group = rank, world, group
         self.hq_l, self.hkv_l = hq // world, hkv // world
         self.q0, self.kv0 = rank * self.hq_l, rank * self.hkv_l
+        self.fused = None  # a FusedHeadGather once enable_fused_gather ran
+
+    def enable_fused_gather(self, max_tokens: int, device) -> "FusedHeadGather":
+        """Gather head outputs from the attention epilogue over NVLink peer
+        memory instead of the NCCL all-gather (bf16 models)."""
+        self.fused = FusedHeadGather(self, max_tokens, device, self.group)
+        return self.fused
 
     def slice_fused_qkv(self, w: torch.Tensor) -> torch.Tensor:
         """Rows of a fused ``q | k | v`` projection weight ``[(Hq + 2 Hkv) D,
@@ -45,3 +52,101 @@ class KvHeadSplit:
         out = torch.empty(self.world * T, ctx.shape[1], dtype=ctx.dtype, device=ctx.device)
         dist.all_gather_into_tensor(out, ctx.contiguous(), group=self.group)
         return out.view(self.world, T, -1).transpose(0, 1).reshape(T, -1)
+
+
+class _DeviceView:
+    """A raw device allocation seen by torch through __cuda_array_interface__
+    (int16 elements, viewed as bf16 by the caller)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class FusedHeadGather:
+    """The head all-gather of a :class:`KvHeadSplit` fused into the
+    attention epilogue (bf16): each rank's attention call stores its heads'
+    output rows straight into every rank's gathered ``[T, Hq * D]`` buffer
+    over NVLink (CUDA IPC peer pointers, no multicast), raises its epoch
+    flag in every rank's flag array, and waits until every rank's flag in
+    its own array has reached the epoch; the replicated output projection
+    then reads the local buffer.  Two buffers alternate by epoch parity.
+    Every rank must make the same sequence of ``attend`` calls."""
+
+    def __init__(self, split: KvHeadSplit, max_tokens: int, device, group=None, limit_cycles: int = 1 << 31):
+        import ctypes as C
+
+        from ._lib import check, lib
+        self.split, self.world, self.rank = split, split.world, split.rank
+        self.width = split.hq * split.D
+        self.max_tokens = max_tokens
+        self.buf_bytes = max_tokens * self.width * 2
+        self.flag_off = 2 * self.buf_bytes
+        self.limit = limit_cycles
+        self.epoch = 0
+        self.device = torch.device(device)
+        ptr = C.c_void_p()
+        check(lib().cevk_ipc_alloc(self.flag_off + 256, C.byref(ptr)))
+        self.own = ptr.value
+        handle = (C.c_char * 64)()
+        check(lib().cevk_ipc_handle(C.c_void_p(self.own), handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bases, self.opened = [], []
+        for i, hb in enumerate(handles):
+            if i == self.rank:
+                self.bases.append(self.own)
+                continue
+            p = C.c_void_p()
+            check(lib().cevk_ipc_open((C.c_char * 64).from_buffer_copy(hb), C.byref(p)))
+            self.bases.append(p.value)
+            self.opened.append(p.value)
+        self.flag_ptrs = (C.c_void_p * self.world)(*[b + self.flag_off for b in self.bases])
+        self.views = [torch.as_tensor(_DeviceView(self.own + k * self.buf_bytes, (max_tokens, self.width)),
+                                      device=self.device).view(torch.bfloat16) for k in (0, 1)]
+        self.group = group
+
+    def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan, scale=None) -> torch.Tensor:
+        """This rank's heads of the packed attention (q [T, Hq/world, D],
+        k / v the rank's arena [S, Hkv/world, D]) gathered with every rank's:
+        returns the local ``[T, Hq * D]`` rows (valid until the call after
+        next)."""
+        import ctypes as C
+        import math
+
+        from . import ops
+        from ._lib import check, lib
+        T, hq, D = q.shape
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens in one call; the gathered buffers hold {self.max_tokens}")
+        if q.dtype != torch.bfloat16 or plan.n_tokens != T:
+            raise ValueError("fused head gather: bf16 and a plan for these tokens")
+        scale = 1.0 / math.sqrt(D) if scale is None else scale
+        self.epoch += 1
+        e = self.epoch
+        off = (e & 1) * self.buf_bytes + self.split.q0 * D * 2
+        dst = (C.c_void_p * self.world)(*[b + off for b in self.bases])
+        ws = plan.workspace
+        s = ops._s()
+        check(lib().cevk_attn_packed_prefill_gather(
+            ops._p(q), ops._p(k), ops._p(v), dst, self.world, T, k.shape[0], hq, k.shape[1], D, q.stride(0),
+            k.stride(0), self.width, ops._p(plan.dev), plan.n_segs, plan.n_tiles, scale, plan.n_split, ops._p(ws),
+            0 if ws is None else ws.numel(), s))
+        check(lib().cevk_gather_signal(self.flag_ptrs, self.world, self.rank, e, s))
+        check(lib().cevk_gather_wait(C.c_void_p(self.own + self.flag_off), self.world, e, self.limit, s))
+        return self.views[e & 1][:T]
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's, once every rank is
+        done writing (call on every rank)."""
+        import ctypes as C
+
+        from ._lib import check, lib
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            check(lib().cevk_ipc_close(C.c_void_p(p)))
+        self.opened = []
+        dist.barrier(group=self.group)
+        self.views = []
+        check(lib().cevk_ipc_free(C.c_void_p(self.own)))

@@ -31,9 +31,9 @@ int check_launch(const char* what) {
   return CEVK_OK;
 }
 
-int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
-                   int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
-                   int n_split, void* workspace, cudaStream_t stream);
+int attn_tc_launch(const void* q, const void* k, const void* v, void* const* o, int n_o, int n_tokens, int n_kv_rows,
+                   int hq, int hkv, int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs,
+                   int n_tiles, float scale, int n_split, void* workspace, cudaStream_t stream);
 int attn_simt_launch(const void* q, const void* k, const void* v, void* o, int hq, int hkv, int D, int q_rs, int kv_rs,
                      int o_rs, const cevk_segment* segs, int n_segs, float scale, cudaStream_t stream);
 
@@ -74,6 +74,10 @@ int cevk_device_status(void) {
       if (r.more[4 * i] == r.info[0])
         len += snprintf(extra + len, sizeof(extra) - len, " [t%d 0x%x p%d]", r.more[4 * i + 1], r.more[4 * i + 2],
                         r.more[4 * i + 3]);
+    if (r.flag == 2)
+      return set_error(CEVK_E_TIMEOUT,
+                       "a bounded device wait gave up (code 2, head all-gather): rank %d's flag reads %d, epoch %d",
+                       r.info[1], r.info[2], r.info[3]);
     return set_error(CEVK_E_TIMEOUT,
                      "a bounded device wait gave up (code %d): block %d thread %d barrier smem offset 0x%x parity %d;"
                      " also stopped in that block:%s",
@@ -142,20 +146,24 @@ int cevk_attn_split_plan(const cevk_segment* segs, int32_t n_segs, int32_t n_til
   return CEVK_OK;
 }
 
-static int packed_prefill(const void* q, const void* k, const void* v, void* o, int32_t n_tokens, int32_t n_kv_rows,
-                          int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride, int32_t kv_row_stride,
-                          int32_t o_row_stride, const cevk_segment* segs_dev, int32_t n_segs, int32_t n_tiles,
-                          float scale, int32_t n_split, void* workspace, int64_t workspace_bytes, int32_t dtype,
-                          void* stream) {
-  if (!q || !k || !v || !o || (!segs_dev && n_segs > 0)) return set_error(CEVK_E_SHAPE, "attention: null pointer");
+static int packed_prefill(const void* q, const void* k, const void* v, void* const* o, int32_t n_o, int32_t n_tokens,
+                          int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
+                          int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev, int32_t n_segs,
+                          int32_t n_tiles, float scale, int32_t n_split, void* workspace, int64_t workspace_bytes,
+                          int32_t dtype, void* stream) {
+  if (!q || !k || !v || !o || n_o < 1 || (!segs_dev && n_segs > 0))
+    return set_error(CEVK_E_SHAPE, "attention: null pointer");
+  for (int i = 0; i < n_o; ++i)
+    if (!o[i]) return set_error(CEVK_E_SHAPE, "attention: null output buffer %d", i);
   if (hkv <= 0 || hq % hkv != 0) return set_error(CEVK_E_SHAPE, "hq (%d) must be a multiple of hkv (%d)", hq, hkv);
   if (q_row_stride < hq * head_dim || o_row_stride < hq * head_dim || kv_row_stride < hkv * head_dim)
     return set_error(CEVK_E_SHAPE, "attention: row stride smaller than heads * head_dim");
   if (n_segs == 0 || n_tiles == 0) return CEVK_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == CEVK_BF16) {
-    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
-      return set_error(CEVK_E_SHAPE, "attention: q/k/v/o must be 16-byte aligned");
+    uintptr_t addr = (uintptr_t)q | (uintptr_t)k | (uintptr_t)v;
+    for (int i = 0; i < n_o; ++i) addr |= (uintptr_t)o[i];
+    if (addr & 15) return set_error(CEVK_E_SHAPE, "attention: q/k/v/o must be 16-byte aligned");
     if ((q_row_stride % 8) || (kv_row_stride % 8) || (o_row_stride % 8))
       return set_error(CEVK_E_SHAPE, "attention: bf16 row strides must be multiples of 8 elements");
     if (128 % (hq / hkv) != 0) return set_error(CEVK_E_SHAPE, "attention: hq/hkv must divide 128");
@@ -168,12 +176,12 @@ static int packed_prefill(const void* q, const void* k, const void* v, void* o, 
                          (long long)need);
       if ((uintptr_t)workspace & 15) return set_error(CEVK_E_SHAPE, "attention: split workspace must be 16-byte aligned");
     }
-    return attn_tc_launch(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
-                          segs_dev, n_segs, n_tiles, scale, n_split, workspace, st);
+    return attn_tc_launch(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride,
+                          o_row_stride, segs_dev, n_segs, n_tiles, scale, n_split, workspace, st);
   }
-  if (dtype == CEVK_F32)
-    return attn_simt_launch(q, k, v, o, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride, segs_dev, n_segs,
-                            scale, st);
+  if (dtype == CEVK_F32 && n_o == 1)
+    return attn_simt_launch(q, k, v, o[0], hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride, segs_dev,
+                            n_segs, scale, st);
   return set_error(CEVK_E_UNSUPPORTED, "attention: dtype %d", dtype);
 }
 
@@ -181,8 +189,8 @@ int cevk_attn_packed_prefill(const void* q, const void* k, const void* v, void* 
                              int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim, int32_t q_row_stride,
                              int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
                              int32_t n_segs, int32_t n_tiles, float scale, int32_t dtype, void* stream) {
-  return packed_prefill(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
-                        segs_dev, n_segs, n_tiles, scale, 1, nullptr, 0, dtype, stream);
+  return packed_prefill(q, k, v, &o, 1, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride,
+                        o_row_stride, segs_dev, n_segs, n_tiles, scale, 1, nullptr, 0, dtype, stream);
 }
 
 int cevk_attn_packed_prefill_split(const void* q, const void* k, const void* v, void* o, int32_t n_tokens,
@@ -190,8 +198,20 @@ int cevk_attn_packed_prefill_split(const void* q, const void* k, const void* v, 
                                    int32_t kv_row_stride, int32_t o_row_stride, const cevk_segment* segs_dev,
                                    int32_t n_segs, int32_t n_tiles, float scale, int32_t n_split, void* workspace,
                                    int64_t workspace_bytes, int32_t dtype, void* stream) {
-  return packed_prefill(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride, o_row_stride,
-                        segs_dev, n_segs, n_tiles, scale, n_split, workspace, workspace_bytes, dtype, stream);
+  return packed_prefill(q, k, v, &o, 1, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride,
+                        o_row_stride, segs_dev, n_segs, n_tiles, scale, n_split, workspace, workspace_bytes, dtype,
+                        stream);
+}
+
+int cevk_attn_packed_prefill_gather(const void* q, const void* k, const void* v, void* const* o_bufs, int32_t n_bufs,
+                                    int32_t n_tokens, int32_t n_kv_rows, int32_t hq, int32_t hkv, int32_t head_dim,
+                                    int32_t q_row_stride, int32_t kv_row_stride, int32_t o_row_stride,
+                                    const cevk_segment* segs_dev, int32_t n_segs, int32_t n_tiles, float scale,
+                                    int32_t n_split, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!o_bufs || n_bufs < 1 || n_bufs > 8) return set_error(CEVK_E_SHAPE, "attention gather: %d buffers (1..8)", n_bufs);
+  return packed_prefill(q, k, v, o_bufs, n_bufs, n_tokens, n_kv_rows, hq, hkv, head_dim, q_row_stride, kv_row_stride,
+                        o_row_stride, segs_dev, n_segs, n_tiles, scale, n_split, workspace, workspace_bytes, CEVK_BF16,
+                        stream);
 }
 
 }  // extern "C"

@@ -75,8 +75,13 @@ struct AttnTc {
   static_assert(SMEM <= 232448, "shared memory");
 };
 
+// Output buffers: every bf16 output row is stored to each of o[0 .. n_o)
+// (one buffer normally; every rank's gathered buffer, through peer
+// pointers, for the fused head all-gather).
+constexpr int kMaxOut = 8;
 struct AttnParams {
-  __nv_bfloat16* o;
+  __nv_bfloat16* o[kMaxOut];
+  int n_o;
   const cevk_segment* segs;
   int n_segs;
   int n_work;   // work tiles = segment tiles x KV heads
@@ -455,8 +460,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tc_fence_after();
       const float inv = 1.f / l_run;
       const bool store = (tq < wk.seg.q_len) && (r / p.group < wk.nt);
-      __nv_bfloat16* orow =
-          p.o + (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D;
+      const size_t orow = (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D;
       float* prow = p.part_o + ((size_t)wk.item * 128 + r) * D;
       if (wk.n_eff > 1 && store) p.part_lse[(size_t)wk.item * 128 + r] = m_run + log2f(l_run);
 #pragma unroll 1
@@ -477,7 +481,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             pv.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
             pv.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
             pv.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c + i) = pv;
+            for (int d = 0; d < p.n_o; ++d) *reinterpret_cast<uint4*>(p.o[d] + orow + c + i) = pv;
           }
         }
       }
@@ -521,8 +525,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnParams p) {
   pv.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
   pv.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
   pv.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
-  *reinterpret_cast<uint4*>(p.o + (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D +
-                            c) = pv;
+  const size_t orow = (size_t)(wk.seg.q_start + tq) * p.o_row_stride + (size_t)(wk.kvh * p.group + h) * D + c;
+  for (int d = 0; d < p.n_o; ++d) *reinterpret_cast<uint4*>(p.o[d] + orow) = pv;
 }
 
 // ---------------------------------------------------------------------------
@@ -557,7 +561,8 @@ static int make_map(CUtensorMap* m, const void* base, int D, int heads, int rows
 }
 
 template <int D, int BN, int KSK, int KSV, int NT>
-static int launch_tc(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
+static int launch_tc(const void* q, const void* k, const void* v, void* const* o, int n_o, int n_tokens, int n_kv_rows,
+                     int hq, int hkv,
                      int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
                      int n_split, void* workspace, cudaStream_t stream) {
   using C = AttnTc<D, BN, KSK, KSV, NT>;
@@ -575,7 +580,9 @@ static int launch_tc(const void* q, const void* k, const void* v, void* o, int n
     attr = true;
   }
   AttnParams prm;
-  prm.o = reinterpret_cast<__nv_bfloat16*>(o);
+  if (n_o < 1 || n_o > kMaxOut) return set_error(CEVK_E_SHAPE, "attention: %d output buffers (1..%d)", n_o, kMaxOut);
+  for (int d = 0; d < kMaxOut; ++d) prm.o[d] = d < n_o ? reinterpret_cast<__nv_bfloat16*>(o[d]) : nullptr;
+  prm.n_o = n_o;
   prm.segs = segs;
   prm.n_segs = n_segs;
   prm.n_work = n_tiles * hkv;
@@ -596,18 +603,19 @@ static int launch_tc(const void* q, const void* k, const void* v, void* o, int n
   return check_launch("attn_combine_kernel");
 }
 
-int attn_tc_launch(const void* q, const void* k, const void* v, void* o, int n_tokens, int n_kv_rows, int hq, int hkv,
+int attn_tc_launch(const void* q, const void* k, const void* v, void* const* o, int n_o, int n_tokens, int n_kv_rows,
+                   int hq, int hkv,
                    int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
                    int n_split, void* workspace, cudaStream_t stream) {
   switch (D) {
     case 64:
-      return launch_tc<64, 64, 6, 4, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
+      return launch_tc<64, 64, 6, 4, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
                                      scale, n_split, workspace, stream);
     case 128:
-      return launch_tc<128, 64, 3, 2, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
+      return launch_tc<128, 64, 3, 2, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
                                       scale, n_split, workspace, stream);
     case 256:
-      return launch_tc<256, 64, 3, 2, 1>(q, k, v, o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
+      return launch_tc<256, 64, 3, 2, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
                                       scale, n_split, workspace, stream);
     default:
       return set_error(CEVK_E_SHAPE, "bf16 attention supports head_dim 64, 128, 256 (got %d)", D);

@@ -1,0 +1,122 @@
+// The cfg5 head all-gather fused into the attention epilogue, over NVLink
+// peer memory (KV-head split of the LFM2 attention layers across ranks).
+//
+// Every rank cudaMallocs its gathered buffers and a flag array, exports them
+// with cudaIpcGetMemHandle and opens its peers' (lazy peer access; no
+// multicast object).  The attention call of rank r stores each output row to
+// every rank's buffer at rank r's head columns (plain 16-byte P2P stores
+// from the epilogue); gather_signal_kernel then raises flag[r] = epoch in
+// every rank's flag array, and gather_wait_kernel on each rank waits (bounded)
+// until all flags of its own array reach the epoch before the replicated
+// output projection reads the buffer.  Replaces the NCCL all-gather of
+// lfm2.rs:145-171's per-head outputs under the KV-head split.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace cevk {
+
+constexpr int kMaxRanks = 8;
+constexpr int kErrGatherTimeout = 2;
+
+struct FlagPtrs {
+  int* p[kMaxRanks];
+};
+
+// Runs after this rank's attention kernel on the same stream: its peer
+// stores are complete; publish them with a system-scope release.
+__global__ void gather_signal_kernel(FlagPtrs flags, int world, int rank, int epoch) {
+  const int i = threadIdx.x;
+  if (i >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.p[i] + rank), "r"(epoch) : "memory");
+}
+
+__global__ void gather_wait_kernel(const int* flags, int world, int epoch, long long limit) {
+  if (threadIdx.x != 0) return;
+  const long long t0 = clock64();
+  for (int s = 0; s < world; ++s) {
+    for (;;) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+      if (v - epoch >= 0) break;  // epochs only grow
+      if (clock64() - t0 > limit) {
+        if (atomicExch(&g_device_error, kErrGatherTimeout) == 0) {
+          g_device_error_info[0] = (int)blockIdx.x;
+          g_device_error_info[1] = s;
+          g_device_error_info[2] = v;
+          g_device_error_info[3] = epoch;
+        }
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+}  // namespace cevk
+
+using namespace cevk;
+
+extern "C" {
+
+int cevk_ipc_alloc(int64_t bytes, void** dev_ptr) {
+  if (!dev_ptr || bytes <= 0) return set_error(CEVK_E_SHAPE, "ipc_alloc: bad arguments");
+  *dev_ptr = nullptr;
+  cudaError_t e = cudaMalloc(dev_ptr, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(*dev_ptr, 0, (size_t)bytes);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "ipc_alloc: %s", cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
+int cevk_ipc_free(void* dev_ptr) {
+  const cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "ipc_free: %s", cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
+int cevk_ipc_handle(const void* dev_ptr, void* handle) {
+  if (!dev_ptr || !handle) return set_error(CEVK_E_SHAPE, "ipc_handle: null argument");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "ipc_handle: %s", cudaGetErrorString(e));
+  static_assert(sizeof(h) == CEVK_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return CEVK_OK;
+}
+
+int cevk_ipc_open(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return set_error(CEVK_E_SHAPE, "ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "ipc_open: %s", cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
+int cevk_ipc_close(void* dev_ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "ipc_close: %s", cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
+int cevk_gather_signal(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch, void* stream) {
+  if (!flags || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || epoch <= 0)
+    return set_error(CEVK_E_SHAPE, "gather_signal: world %d rank %d epoch %d", world, rank, epoch);
+  FlagPtrs f{};
+  for (int i = 0; i < world; ++i) {
+    if (!flags[i]) return set_error(CEVK_E_SHAPE, "gather_signal: null flag array %d", i);
+    f.p[i] = flags[i];
+  }
+  gather_signal_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(f, world, rank, epoch);
+  return check_launch("gather_signal_kernel");
+}
+
+int cevk_gather_wait(const int32_t* flags, int32_t world, int32_t epoch, int64_t limit_cycles, void* stream) {
+  if (!flags || world < 1 || world > kMaxRanks || epoch <= 0 || limit_cycles <= 0)
+    return set_error(CEVK_E_SHAPE, "gather_wait: world %d epoch %d", world, epoch);
+  gather_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, world, epoch, limit_cycles);
+  return check_launch("gather_wait_kernel");
+}
+
+}  // extern "C"

@@ -71,3 +71,54 @@ def test_lfm2_kv_head_split_matches_unsplit():
         assert p.exitcode == 0
     res = dict(q.get(timeout=10) for _ in range(2))
     assert res[0] is not None and res[0] < 1e-4, res
+
+
+def _rank_fused(rank, world, port, q):
+    """bf16: the split engine with the fused head gather (attention epilogue
+    stores into every rank's buffer over NVLink) against the same split
+    engine with the NCCL all-gather: same kernels, same bits."""
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=timedelta(seconds=60))
+    fused = None
+    try:
+        from cev_b200 import configs, hybrid, weights
+        from cev_b200.tp import KvHeadSplit
+        cfg = configs.tiny_lfm2()
+        w = weights.init_weights(cfg, 42)
+        D = cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"]
+        dev = f"cuda:{rank}"
+        sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
+        nccl = _run(hybrid.Lfm2(cfg, w, torch.bfloat16, dev, arena_rows=4096, split=sp), cfg)
+        sp2 = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
+        fused = sp2.enable_fused_gather(1024, dev)
+        got = _run(hybrid.Lfm2(cfg, w, torch.bfloat16, dev, arena_rows=4096, split=sp2), cfg)
+        from cev_b200 import ops
+        ops.device_status()
+        q.put((rank, (got - nccl).abs().max().item(), fused.epoch))
+    finally:
+        if fused is not None:
+            fused.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_lfm2_fused_head_gather_matches_nccl_gather():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank_fused, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    res = {r: (err, ep) for r, err, ep in (q.get(timeout=10) for _ in range(2))}
+    for r in (0, 1):
+        err, epochs = res[r]
+        assert epochs > 0 and err == 0.0, res
