@@ -8,14 +8,23 @@
 // row; the warp holds the row in shared memory so the rotation partner
 // (d +- rot/2) can live in any lane.  HBM-bound: each element is read once
 // and written once.
+#include <cmath>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace cevk {
 
+// 1f32 / (theta^(2i/rot) as f32) for i < rot/2, the power in f64 on the
+// host (qwen3.rs:109-112): the same for every token, passed by value.
+struct InvFreq {
+  float v[256];
+};
+
 template <typename T>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const T* __restrict__ qkv, int row_stride, int q_head_stride, int k_col, int v_col, const T* __restrict__ qw,
-    const T* __restrict__ kw, float eps, int plus_one, const int32_t* __restrict__ pos, double theta, int rot,
+    const T* __restrict__ kw, float eps, int plus_one, const int32_t* __restrict__ pos, const InvFreq inv, int rot,
     T* __restrict__ q_out, T* __restrict__ k_arena, T* __restrict__ v_arena, int kv_rs, const int32_t* __restrict__ kv_rows,
     int hq, int hkv, int D) {
   // One block per token: cos/sin of its position are computed once and
@@ -29,9 +38,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float p = (float)pos[t];
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    // 1f32 / (theta^(2i/rot) as f32), the power in f64 (qwen3.rs:109-112).
-    const float inv = 1.0f / (float)pow(theta, (double)(2 * i) / (double)rot);
-    const float ang = p * inv;
+    const float ang = p * inv.v[i];
     cs[i] = cosf(ang);
     sn[i] = sinf(ang);
   }
@@ -84,6 +91,128 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   }
 }
 
+// E consecutive elements per lane (E = head_dim / 32), one vector access.
+template <typename T, int E>
+__device__ __forceinline__ void load_row(const T* __restrict__ p, float* x) {
+  constexpr int BYTES = E * (int)sizeof(T);
+  static_assert(BYTES == 2 || BYTES % 4 == 0, "vector width");
+  if constexpr (BYTES == 2) {
+    x[0] = to_f(*p);
+  } else if constexpr (BYTES <= 16) {
+    using V = typename std::conditional<BYTES == 4, uint32_t, typename std::conditional<BYTES == 8, uint2, uint4>::type>::type;
+    V v = *reinterpret_cast<const V*>(p);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < E; ++i) x[i] = to_f(e[i]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < BYTES / 16; ++c) {
+      uint4 v = reinterpret_cast<const uint4*>(p)[c];
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int i = 0; i < 16 / (int)sizeof(T); ++i) x[c * (16 / (int)sizeof(T)) + i] = to_f(e[i]);
+    }
+  }
+}
+template <typename T, int E>
+__device__ __forceinline__ void store_row(T* __restrict__ p, const float* y) {
+  constexpr int BYTES = E * (int)sizeof(T);
+  if constexpr (BYTES == 2) {
+    *p = from_f<T>(y[0]);
+  } else if constexpr (BYTES <= 16) {
+    using V = typename std::conditional<BYTES == 4, uint32_t, typename std::conditional<BYTES == 8, uint2, uint4>::type>::type;
+    V v;
+    T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int i = 0; i < E; ++i) e[i] = from_f<T>(y[i]);
+    *reinterpret_cast<V*>(p) = v;
+  } else {
+#pragma unroll
+    for (int c = 0; c < BYTES / 16; ++c) {
+      uint4 v;
+      T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+      for (int i = 0; i < 16 / (int)sizeof(T); ++i) e[i] = from_f<T>(y[c * (16 / (int)sizeof(T)) + i]);
+      reinterpret_cast<uint4*>(p)[c] = v;
+    }
+  }
+}
+
+// The same computation with each head row held in registers, E = D / 32
+// consecutive elements per lane (one vector load / store), and the rotation
+// partner (d +- rot/2, in lane +- rot/2/E with the same element slot) taken
+// by a warp shuffle: no shared-memory round trip per head, so a warp's head
+// rows are independent and their loads overlap.
+template <typename T, int E>
+__global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
+    const T* __restrict__ qkv, int row_stride, int q_head_stride, int k_col, int v_col, const T* __restrict__ qw,
+    const T* __restrict__ kw, float eps, int plus_one, const int32_t* __restrict__ pos, const InvFreq inv, int rot,
+    T* __restrict__ q_out, T* __restrict__ k_arena, T* __restrict__ v_arena, int kv_rs, const int32_t* __restrict__ kv_rows,
+    int hq, int hkv) {
+  constexpr int D = 32 * E;
+  __shared__ float cs[256], sn[256];
+  const int half = rot / 2;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float p = (float)pos[t];
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float ang = p * inv.v[i];
+    cs[i] = cosf(ang);
+    sn[i] = sinf(ang);
+  }
+  __syncthreads();
+  const int d0 = lane * E;
+  const int hop = half / E;  // lanes between rotation partners
+  const int partner = d0 < half ? lane + hop : (d0 < rot ? lane - hop : lane);
+  float c[E], s[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int d = d0 + e;
+    const int i = d < half ? d : d - half;
+    c[e] = d < rot ? cs[i] : 1.f;
+    s[e] = d < rot ? (d < half ? -sn[i] : sn[i]) : 0.f;
+  }
+  float qwv[E], kwv[E];
+  load_row<T, E>(qw + d0, qwv);
+  load_row<T, E>(kw + d0, kwv);
+  const float add = plus_one ? 1.f : 0.f;
+  const size_t kv_row = (size_t)kv_rows[t];
+  const int heads = hq + 2 * hkv;
+#pragma unroll 2
+  for (int h = warp; h < heads; h += 8) {
+    const T* src;
+    T* dst;
+    if (h < hq) {
+      src = qkv + (size_t)t * row_stride + (size_t)h * q_head_stride;
+      dst = q_out + ((size_t)t * hq + h) * D;
+    } else if (h < hq + hkv) {
+      src = qkv + (size_t)t * row_stride + k_col + (size_t)(h - hq) * D;
+      dst = k_arena + kv_row * kv_rs + (size_t)(h - hq) * D;
+    } else {
+      src = qkv + (size_t)t * row_stride + v_col + (size_t)(h - hq - hkv) * D;
+      dst = v_arena + kv_row * kv_rs + (size_t)(h - hq - hkv) * D;
+    }
+    float x[E];
+    load_row<T, E>(src + d0, x);
+    if (h < hq + hkv) {  // warp-uniform
+      const float* w = h < hq ? qwv : kwv;
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+      const float r = rsqrtf(warp_sum(ss) / D + eps);
+      // Like the reference, the normed value is in the model dtype before RoPE.
+#pragma unroll
+      for (int e = 0; e < E; ++e) x[e] = to_f(from_f<T>(x[e] * r * (w[e] + add)));
+      float y[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) y[e] = x[e] * c[e] + __shfl_sync(0xffffffffu, x[e], partner) * s[e];
+      store_row<T, E>(dst + d0, y);
+    } else {
+      store_row<T, E>(dst + d0, x);  // V: a plain copy into the arena
+    }
+  }
+}
+
 }  // namespace cevk
 
 using namespace cevk;
@@ -99,19 +228,48 @@ extern "C" int cevk_qk_norm_rope(const void* qkv, int32_t row_stride, int32_t q_
   if (head_dim <= 0 || head_dim > 512 || rotary_dim < 0 || rotary_dim > head_dim || (rotary_dim & 1))
     return set_error(CEVK_E_SHAPE, "qk_norm_rope: head_dim %d / rotary_dim %d", head_dim, rotary_dim);
   if (kv_row_stride < hkv * head_dim) return set_error(CEVK_E_SHAPE, "qk_norm_rope: kv row stride too small");
+  if (rotary_dim / 2 > 256) return set_error(CEVK_E_SHAPE, "qk_norm_rope: rotary_dim %d above 512", rotary_dim);
   if (n_tokens <= 0) return CEVK_OK;
+  InvFreq inv{};
+  for (int i = 0; i < rotary_dim / 2; ++i)
+    inv.v[i] = 1.0f / (float)std::pow(theta, (double)(2 * i) / (double)rotary_dim);
   const unsigned blocks = (unsigned)n_tokens;
   const size_t smem = (rotary_dim + 8 * head_dim) * sizeof(float);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Vector path: head_dim 64 / 128 / 256, rotation partners in lanes with
+  // the same element slot, every row start aligned to the vector width.
+  const int E = head_dim / 32, es = dtype == CEVK_BF16 ? 2 : 4;
+  const bool vec = (head_dim == 64 || head_dim == 128 || head_dim == 256) && (rotary_dim / 2) % E == 0 &&
+                   row_stride % E == 0 && q_head_stride % E == 0 && k_col % E == 0 && v_col % E == 0 &&
+                   kv_row_stride % E == 0 &&
+                   (((uintptr_t)qkv | (uintptr_t)q_out | (uintptr_t)k_arena | (uintptr_t)v_arena |
+                     (uintptr_t)q_norm_w | (uintptr_t)k_norm_w) % (E * es)) == 0;
+  if (vec && (dtype == CEVK_BF16 || dtype == CEVK_F32)) {
+#define CEVK_ROPE_VEC(TT, EE)                                                                                          \
+  qk_norm_rope_vec_kernel<TT, EE><<<blocks, 256, 0, st>>>(                                                             \
+      (const TT*)qkv, row_stride, q_head_stride, k_col, v_col, (const TT*)q_norm_w, (const TT*)k_norm_w, eps,          \
+      norm_plus_one, pos, inv, rotary_dim, (TT*)q_out, (TT*)k_arena, (TT*)v_arena, kv_row_stride, kv_rows, hq, hkv)
+    if (dtype == CEVK_BF16) {
+      if (E == 2) CEVK_ROPE_VEC(__nv_bfloat16, 2);
+      else if (E == 4) CEVK_ROPE_VEC(__nv_bfloat16, 4);
+      else CEVK_ROPE_VEC(__nv_bfloat16, 8);
+    } else {
+      if (E == 2) CEVK_ROPE_VEC(float, 2);
+      else if (E == 4) CEVK_ROPE_VEC(float, 4);
+      else CEVK_ROPE_VEC(float, 8);
+    }
+#undef CEVK_ROPE_VEC
+    return check_launch("qk_norm_rope_vec_kernel");
+  }
   if (dtype == CEVK_BF16) {
     qk_norm_rope_kernel<__nv_bfloat16><<<blocks, 256, smem, st>>>(
         (const __nv_bfloat16*)qkv, row_stride, q_head_stride, k_col, v_col, (const __nv_bfloat16*)q_norm_w,
-        (const __nv_bfloat16*)k_norm_w, eps, norm_plus_one, pos, theta, rotary_dim, (__nv_bfloat16*)q_out,
+        (const __nv_bfloat16*)k_norm_w, eps, norm_plus_one, pos, inv, rotary_dim, (__nv_bfloat16*)q_out,
         (__nv_bfloat16*)k_arena, (__nv_bfloat16*)v_arena, kv_row_stride, kv_rows, hq, hkv, head_dim);
   } else if (dtype == CEVK_F32) {
     qk_norm_rope_kernel<float><<<blocks, 256, smem, st>>>(
         (const float*)qkv, row_stride, q_head_stride, k_col, v_col, (const float*)q_norm_w, (const float*)k_norm_w, eps,
-        norm_plus_one, pos, theta, rotary_dim, (float*)q_out, (float*)k_arena, (float*)v_arena, kv_row_stride, kv_rows,
+        norm_plus_one, pos, inv, rotary_dim, (float*)q_out, (float*)k_arena, (float*)v_arena, kv_row_stride, kv_rows,
         hq, hkv, head_dim);
   } else {
     return set_error(CEVK_E_UNSUPPORTED, "qk_norm_rope: dtype %d", dtype);
