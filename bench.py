@@ -352,7 +352,7 @@ def op_bench(args, dev):
                 "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
                 "config": {"workload": f"B{B} T{T} nk{nk} nv{nv} dk{dk} dv{dv}, chunk 64, state in/out",
                            "flop_per_step": flops, "bytes_per_step": nbytes},
-                "roofline": {"bound": "latency (sequential chunk scan, mma.sync split TF32)", "achieved": tf,
+                "roofline": {"bound": "mma.sync issue rate (bf16 three-term split)", "achieved": tf,
                              "unit": "TFLOP/s",
                              "hbm_gbs": nbytes / (ms / 1e3) / 1e9, "hbm_peak_gbs": peak_hbm, "peak_source": src}}
     elif args.op == "conv":

@@ -1,18 +1,21 @@
 // Gated DeltaNet chunked prefill on tensor cores (bf16 models): the same
 // chunked delta rule as gdn.cu (qwen35.rs:301-368), split into a
 // chunk-parallel phase and the sequential state scan, with every matrix
-// product on the tensor cores in split TF32 (mma.sync m16n8k8, f32
-// accumulate; x = hi + lo, three products hi*hi + hi*lo + lo*hi), which keeps
-// them at f32 accuracy: the reference runs the delta rule in f32, the state
-// carries every chunk's error forward, and a bf16 model amplifies small
-// output differences layer by layer (plain TF32 on the output-only products
-// measured at the edge of the model-level bound).
+// product on the tensor cores as a bf16 three-term split (mma.sync m16n8k16,
+// f32 accumulate; x = hi + lo with hi = bf16(x), lo = bf16(x - hi), three
+// products hi*hi + hi*lo + lo*hi): about 16 significant bits per operand
+// instead of plain bf16's 8, because the reference runs the delta rule in
+// f32, the state carries every chunk's error forward, and a bf16 model
+// amplifies small output differences layer by layer.  These kernels are
+// bound by the mma.sync issue rate, so the split's MMA count is the cost: a
+// TF32 split at K = 8 (about 22 bits) needed twice the instructions and
+// measured 1.35x slower for both kernels together.
 //
 // gdn_prep_kernel -- one CTA per (chunk of 64 tokens, value head, row):
 //   q, k <- l2norm (q * dk^-1/2); beta = sigmoid(b); g = -exp(A_log) *
 //   softplus(a + dt_bias); cum = cumsum(g) over the chunk;
 //   A = strict_lower(beta_i k_i.k_j e^(cum_i - cum_j)), T = (I + A)^-1 by
-//   forward substitution; intra = lower(q_i.k_j e^(cum_i - cum_j));
+//   recursive block inversion; intra = lower(q_i.k_j e^(cum_i - cum_j));
 //   W = T (k beta e^cum), U = T (v beta), q' = q e^cum, k' = k e^(last - cum).
 //   All of it to the workspace (f32).
 // gdn_scan_kernel -- one CTA per (value head, 32 value columns, row), over
@@ -29,99 +32,93 @@ namespace gtc {
 constexpr int C = 64;   // chunk length (qwen35.rs:302)
 constexpr int VS = 32;  // value columns per scan CTA
 
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
-// D += A(16x8, row) * B(8x8, col), TF32 in, f32 accumulate.
-__device__ __forceinline__ void mma_tf32(float* d, const uint32_t* a, const uint32_t* b) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-
-// Fragments of m16n8k8 (lane = 4 * gid + tig):
-//   A: a0 (gid, tig), a1 (gid+8, tig), a2 (gid, tig+4), a3 (gid+8, tig+4)
-//   B: b0 (k = tig, n = gid), b1 (k = tig+4, n = gid)
-//   D: d0 (gid, 2tig), d1 (gid, 2tig+1), d2 (gid+8, 2tig), d3 (gid+8, 2tig+1)
-// SPLIT: x = hi + lo in TF32, D += hi*hi + hi*lo + lo*hi.
-template <bool SPLIT>
-struct Frag {
-  uint32_t hi[4], lo[4];
-  __device__ __forceinline__ void set(int i, float x) {
-    hi[i] = to_tf32(x);
-    if (SPLIT) lo[i] = to_tf32(x - __uint_as_float(hi[i]));
-  }
-};
-template <bool SPLIT>
-__device__ __forceinline__ void mma(float* d, const Frag<SPLIT>& a, const Frag<SPLIT>& b) {
-  mma_tf32(d, a.hi, b.hi);
-  if (SPLIT) {
-    mma_tf32(d, a.hi, b.lo);
-    mma_tf32(d, a.lo, b.hi);
-  }
-}
-// An m16n8 accumulator whose split products run as three independent
-// chains (hi*hi, hi*lo, lo*hi), summed when read: a third of the dependent
-// MMA latency of accumulating all three into one register set.
-template <bool SPLIT>
+// An m16n8 accumulator whose three split products run as independent chains
+// (hi*hi, hi*lo, lo*hi), summed when read.
 struct Acc {
   float d[4], c[4], e[4];
   __device__ __forceinline__ void zero() {
 #pragma unroll
     for (int i = 0; i < 4; ++i) d[i] = c[i] = e[i] = 0.f;
   }
-  __device__ __forceinline__ float get(int i) const { return SPLIT ? d[i] + (c[i] + e[i]) : d[i]; }
+  __device__ __forceinline__ float get(int i) const { return d[i] + (c[i] + e[i]); }
 };
-template <bool SPLIT>
-__device__ __forceinline__ void mma(Acc<SPLIT>& acc, const Frag<SPLIT>& a, const Frag<SPLIT>& b) {
-  mma_tf32(acc.d, a.hi, b.hi);
-  if (SPLIT) {
-    mma_tf32(acc.c, a.hi, b.lo);
-    mma_tf32(acc.e, a.lo, b.hi);
-  }
+// Fragments of m16n8k16 (lane = 4 * gid + tig), two bf16 per register,
+// lower k first; D as for every m16n8 shape:
+//   A: a0 (gid, 2tig..+1), a1 (gid+8, 2tig..+1), a2 (gid, 2tig+8..+9), a3 (gid+8, 2tig+8..+9)
+//   B: b0 (k = 2tig..+1, n = gid), b1 (k = 2tig+8..+9, n = gid)
+//   D: d0 (gid, 2tig), d1 (gid, 2tig+1), d2 (gid+8, 2tig), d3 (gid+8, 2tig+1)
+struct FragH {
+  uint32_t hi[4], lo[4];
+};
+__device__ __forceinline__ void split_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(x0, x1);
+  lo = pack_bf16x2(x0 - __uint_as_float(hi << 16), x1 - __uint_as_float(hi & 0xffff0000u));
 }
-// A fragment of a row-major matrix M (pitch ld) at (r0, k0), optionally with
-// a per-column scale.
-template <bool SPLIT>
-__device__ __forceinline__ Frag<SPLIT> frag_a(const float* M, int ld, int r0, int k0, int gid, int tig) {
-  Frag<SPLIT> f;
-  f.set(0, M[(r0 + gid) * ld + k0 + tig]);
-  f.set(1, M[(r0 + gid + 8) * ld + k0 + tig]);
-  f.set(2, M[(r0 + gid) * ld + k0 + tig + 4]);
-  f.set(3, M[(r0 + gid + 8) * ld + k0 + tig + 4]);
+__device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+__device__ __forceinline__ void mma16(Acc& acc, const FragH& a, const FragH& b) {
+  mma_bf16(acc.d, a.hi, b.hi);
+  mma_bf16(acc.c, a.hi, b.lo);
+  mma_bf16(acc.e, a.lo, b.hi);
+}
+// The three products into one register set (the prep kernel's accumulators).
+__device__ __forceinline__ void mma16(float* d, const FragH& a, const FragH& b) {
+  mma_bf16(d, a.hi, b.hi);
+  mma_bf16(d, a.hi, b.lo);
+  mma_bf16(d, a.lo, b.hi);
+}
+// A (16 x 16) from row-major M at (r0, k0).
+__device__ __forceinline__ FragH frag_a16(const float* M, int ld, int r0, int k0, int gid, int tig) {
+  FragH f;
+  const float* p0 = M + (r0 + gid) * ld + k0 + 2 * tig;
+  const float* p1 = p0 + 8 * ld;
+  const float2 v0 = *reinterpret_cast<const float2*>(p0), v1 = *reinterpret_cast<const float2*>(p1);
+  const float2 v2 = *reinterpret_cast<const float2*>(p0 + 8), v3 = *reinterpret_cast<const float2*>(p1 + 8);
+  split_bf16(v0.x, v0.y, f.hi[0], f.lo[0]);
+  split_bf16(v1.x, v1.y, f.hi[1], f.lo[1]);
+  split_bf16(v2.x, v2.y, f.hi[2], f.lo[2]);
+  split_bf16(v3.x, v3.y, f.hi[3], f.lo[3]);
   return f;
 }
-// A fragment of the transpose of row-major M: A(r, k) = M[k][r].
-template <bool SPLIT>
-__device__ __forceinline__ Frag<SPLIT> frag_at(const float* M, int ld, int r0, int k0, int gid, int tig) {
-  Frag<SPLIT> f;
-  f.set(0, M[(k0 + tig) * ld + r0 + gid]);
-  f.set(1, M[(k0 + tig) * ld + r0 + gid + 8]);
-  f.set(2, M[(k0 + tig + 4) * ld + r0 + gid]);
-  f.set(3, M[(k0 + tig + 4) * ld + r0 + gid + 8]);
+// A (16 x 16) = the transpose of row-major M: A(r, k) = M[k][r].
+__device__ __forceinline__ FragH frag_at16(const float* M, int ld, int r0, int k0, int gid, int tig) {
+  FragH f;
+  const float* p = M + (k0 + 2 * tig) * ld + r0 + gid;
+  split_bf16(p[0], p[ld], f.hi[0], f.lo[0]);
+  split_bf16(p[8], p[ld + 8], f.hi[1], f.lo[1]);
+  split_bf16(p[8 * ld], p[9 * ld], f.hi[2], f.lo[2]);
+  split_bf16(p[8 * ld + 8], p[9 * ld + 8], f.hi[3], f.lo[3]);
   return f;
 }
-// B fragment where B(k, n) = M[k][n] (row-major [K][N]); with row scale s[k].
-template <bool SPLIT>
-__device__ __forceinline__ Frag<SPLIT> frag_b(const float* M, int ld, int k0, int n0, int gid, int tig,
-                                              const float* s = nullptr) {
-  Frag<SPLIT> f;
-  const float x0 = M[(k0 + tig) * ld + n0 + gid], x1 = M[(k0 + tig + 4) * ld + n0 + gid];
-  f.set(0, s ? x0 * s[k0 + tig] : x0);
-  f.set(1, s ? x1 * s[k0 + tig + 4] : x1);
+// B (16 x 8) with B(k, n) = M[k][n] (row-major [K][N]).
+__device__ __forceinline__ FragH frag_b16(const float* M, int ld, int k0, int n0, int gid, int tig) {
+  FragH f;
+  const float* p = M + (k0 + 2 * tig) * ld + n0 + gid;
+  split_bf16(p[0], p[ld], f.hi[0], f.lo[0]);
+  split_bf16(p[8 * ld], p[9 * ld], f.hi[1], f.lo[1]);
   return f;
 }
-// B fragment where B(k, n) = M[n][k] (B = M^T, M row-major [N][K]).
-template <bool SPLIT>
-__device__ __forceinline__ Frag<SPLIT> frag_bt(const float* M, int ld, int k0, int n0, int gid, int tig) {
-  Frag<SPLIT> f;
-  f.set(0, M[(n0 + gid) * ld + k0 + tig]);
-  f.set(1, M[(n0 + gid) * ld + k0 + tig + 4]);
+// B (16 x 8) with B(k, n) = M[k][n] * s[k].
+__device__ __forceinline__ FragH frag_b16s(const float* M, int ld, int k0, int n0, int gid, int tig, const float* s) {
+  FragH f;
+  const int k = k0 + 2 * tig;
+  const float* p = M + k * ld + n0 + gid;
+  split_bf16(p[0] * s[k], p[ld] * s[k + 1], f.hi[0], f.lo[0]);
+  split_bf16(p[8 * ld] * s[k + 8], p[9 * ld] * s[k + 9], f.hi[1], f.lo[1]);
+  return f;
+}
+// B (16 x 8) with B(k, n) = M[n][k] (B = M^T, M row-major [N][K]).
+__device__ __forceinline__ FragH frag_bt16(const float* M, int ld, int k0, int n0, int gid, int tig) {
+  FragH f;
+  const float* p = M + (n0 + gid) * ld + k0 + 2 * tig;
+  const float2 v0 = *reinterpret_cast<const float2*>(p), v1 = *reinterpret_cast<const float2*>(p + 8);
+  split_bf16(v0.x, v0.y, f.hi[0], f.lo[0]);
+  split_bf16(v1.x, v1.y, f.hi[1], f.lo[1]);
   return f;
 }
 
@@ -268,15 +265,15 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) ak[n][e] = aq[n][e] = 0.f;
 #pragma unroll 1
-    for (int k0 = 0; k0 < DK; k0 += 8) {
-      const Frag<true> fk = frag_a<true>(sK, KP, r0, k0, gid, tig);
-      const Frag<true> fq = frag_a<true>(sQ, KP, r0, k0, gid, tig);
+    for (int k0 = 0; k0 < DK; k0 += 16) {
+      const FragH fk = frag_a16(sK, KP, r0, k0, gid, tig);
+      const FragH fq = frag_a16(sQ, KP, r0, k0, gid, tig);
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         if (n * 8 > r0 + 15) continue;  // strictly above the diagonal block
-        const Frag<true> fb = frag_bt<true>(sK, KP, k0, n * 8, gid, tig);
-        mma<true>(ak[n], fk, fb);
-        mma<true>(aq[n], fq, fb);
+        const FragH fb = frag_bt16(sK, KP, k0, n * 8, gid, tig);
+        mma16(ak[n], fk, fb);
+        mma16(aq[n], fq, fb);
       }
     }
     float* intra = p.intra + ci * C * C;
@@ -330,19 +327,16 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
     }
   }
   __syncthreads();
-  // 16 x 16 tile = A (16 x K) * B (K x 16), split TF32, into acc[2][4] (D layout)
+  // 16 x 16 tile = A (16 x K) * B (K x 16), split bf16, into acc[2][4] (D layout)
   auto mm16 = [&](const float* A, int lda, const float* B, int ldb, int K, float (*acc)[4]) {
 #pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
-    for (int k0 = 0; k0 < K; k0 += 8) {
-      const Frag<true> fa = frag_a<true>(A, lda, 0, k0, gid, tig);
+    for (int k0 = 0; k0 < K; k0 += 16) {
+      const FragH fa = frag_a16(A, lda, 0, k0, gid, tig);
 #pragma unroll
-      for (int n = 0; n < 2; ++n) {
-        const Frag<true> fb = frag_b<true>(B, ldb, k0, n * 8, gid, tig);
-        mma<true>(acc[n], fa, fb);
-      }
+      for (int n = 0; n < 2; ++n) mma16(acc[n], fa, frag_b16(B, ldb, k0, n * 8, gid, tig));
     }
   };
   auto put16 = [&](float* D, int ldd, const float (*acc)[4], float sgn) {
@@ -398,13 +392,10 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
 #pragma unroll 1
-      for (int k0 = 0; k0 < kend; k0 += 8) {
-        const Frag<true> fa = frag_a<true>(sT, AP, r0, k0, gid, tig);
+      for (int k0 = 0; k0 < kend; k0 += 16) {
+        const FragH fa = frag_a16(sT, AP, r0, k0, gid, tig);
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const Frag<true> fb = frag_b<true>(src, KP, k0, cb + n * 8, gid, tig, scale);
-          mma<true>(acc[n], fa, fb);
-        }
+        for (int n = 0; n < 8; ++n) mma16(acc[n], fa, frag_b16s(src, KP, k0, cb + n * 8, gid, tig, scale));
       }
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
@@ -417,14 +408,18 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 }
 
 // ---------------------------------------------------------------------------
-// 8 warps: warp w computes rows 16 (w & 3) .. +16 of v_new / out for value
-// columns 16 (w >> 2) .. +16 of the slice, and state rows 16 w .. +16 in the
-// update (warps 0 .. dk/16 - 1).
-constexpr int SCAN_THREADS = 256;
+// 16 warps in two groups of 8; within a group warp w covers rows 16 (w & 3)
+// .. +16 and value columns 16 (w >> 2) .. +16 of the 64 x 32 chunk block.
+//   group 0: W S, then v_new = U - W S, then the state update S = e^last S +
+//            k'^T v_new for state rows 16 w .. +16 (w < dk/16);
+//   group 1: q' S, then out = q' S + intra v_new and its store.
+// After v_new is in shared memory the update and the output run side by
+// side, so a chunk's dependent chain is one product shorter on each side.
+constexpr int SCAN_THREADS = 512;
 template <int DK, int DV>
 __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
   constexpr int KP = DK + 4, SP = VS + 8, AP = C + 4;
-  static_assert(DK % 16 == 0 && DK / 16 <= SCAN_THREADS / 32, "16 state rows per warp");
+  static_assert(DK % 16 == 0 && DK / 16 <= 8, "16 state rows per warp of group 0");
   extern __shared__ float sm[];
   // k', U and intra are double-buffered: chunk ch + 1's copies stream in
   // while chunk ch computes (W and q' follow once W S and q' S are done).
@@ -437,7 +432,8 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int sl = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int c0 = sl * VS;
-  const int r0 = (warp & 3) * 16, n0 = (warp >> 2) * 16;  // rows / columns of v_new and out
+  const int grp = warp >> 3, w8 = warp & 7;
+  const int r0 = (w8 & 3) * 16, n0 = (w8 >> 2) * 16;  // rows / columns of v_new and out
 
   for (int i = tid; i < DK * VS; i += SCAN_THREADS) {
     const int d = i / VS, c = i % VS;
@@ -489,59 +485,52 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
     __syncthreads();
     if (ch + 1 < p.n_chunks) load_rest(chunk_index(p, b, ch + 1, h), buf ^ 1);
     const float el = p.elast[ci];
-    Acc<true> vn[2], o[2];
+    // group 0: W S; group 1: q' S (over dk)
+    Acc acc2[2];
 #pragma unroll
-    for (int n = 0; n < 2; ++n) {
-      vn[n].zero();
-      o[n].zero();
-    }
-    // W S and q' S over dk
+    for (int n = 0; n < 2; ++n) acc2[n].zero();
+    const float* sA = grp == 0 ? sW : sQp;
 #pragma unroll 2
-    for (int k0 = 0; k0 < DK; k0 += 8) {
-      const Frag<true> fw = frag_a<true>(sW, KP, r0, k0, gid, tig);
-      const Frag<true> fq = frag_a<true>(sQp, KP, r0, k0, gid, tig);
+    for (int k0 = 0; k0 < DK; k0 += 16) {
+      const FragH fa = frag_a16(sA, KP, r0, k0, gid, tig);
 #pragma unroll
-      for (int n = 0; n < 2; ++n) {
-        const Frag<true> fs = frag_b<true>(sS, SP, k0, n0 + n * 8, gid, tig);
-        mma<true>(vn[n], fw, fs);
-        mma<true>(o[n], fq, fs);
-      }
+      for (int n = 0; n < 2; ++n) mma16(acc2[n], fa, frag_b16(sS, SP, k0, n0 + n * 8, gid, tig));
     }
-    // v_new = U - W S (in place over U: each warp owns its 16 x 16 block)
+    if (grp == 0) {
+      // v_new = U - W S (in place over U: each warp owns its 16 x 16 block)
 #pragma unroll
-    for (int n = 0; n < 2; ++n)
+      for (int n = 0; n < 2; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = r0 + gid + (e >> 1) * 8, j = n0 + n * 8 + 2 * tig + (e & 1);
-        sU[i * SP + j] -= vn[n].get(e);
-      }
+        for (int e = 0; e < 4; ++e) {
+          const int i = r0 + gid + (e >> 1) * 8, j = n0 + n * 8 + 2 * tig + (e & 1);
+          sU[i * SP + j] -= acc2[n].get(e);
+        }
+    }
     __syncthreads();
     // W and q' are done for this chunk: the next chunk's stream in behind
-    // the intra and state-update phases.
+    // the output and state-update phases.
     if (ch + 1 < p.n_chunks) load_wq(chunk_index(p, b, ch + 1, h));
-    // out = q' S + intra v_new (intra lower triangular)
+    if (grp == 1) {
+      // out = q' S + intra v_new (intra lower triangular)
 #pragma unroll 1
-    for (int k0 = 0; k0 < r0 + 16; k0 += 8) {
-      const Frag<true> fi = frag_a<true>(sI, AP, r0, k0, gid, tig);
+      for (int k0 = 0; k0 < r0 + 16; k0 += 16) {
+        const FragH fi = frag_a16(sI, AP, r0, k0, gid, tig);
 #pragma unroll
-      for (int n = 0; n < 2; ++n) {
-        const Frag<true> fv = frag_b<true>(sU, SP, k0, n0 + n * 8, gid, tig);
-        mma<true>(o[n], fi, fv);
+        for (int n = 0; n < 2; ++n) mma16(acc2[n], fi, frag_b16(sU, SP, k0, n0 + n * 8, gid, tig));
       }
-    }
 #pragma unroll
-    for (int n = 0; n < 2; ++n)
+      for (int n = 0; n < 2; ++n)
 #pragma unroll
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        const int t = ch * C + r0 + gid + hlf * 8;
-        if (t < p.T)
-          *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n0 + n * 8 + 2 * tig) =
-              make_float2(o[n].get(2 * hlf), o[n].get(2 * hlf + 1));
-      }
-    // S = e^last S + k'^T v_new: warp w owns state rows 16 w .. 16 w + 15
-    if (warp < DK / 16) {
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          const int t = ch * C + r0 + gid + hlf * 8;
+          if (t < p.T)
+            *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n0 + n * 8 + 2 * tig) =
+                make_float2(acc2[n].get(2 * hlf), acc2[n].get(2 * hlf + 1));
+        }
+    } else if (warp < DK / 16) {
+      // S = e^last S + k'^T v_new: warp w owns state rows 16 w .. 16 w + 15
       const int d0 = warp * 16;
-      Acc<true> acc[4];
+      Acc acc[4];
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
         acc[n].zero();
@@ -552,13 +541,10 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
         }
       }
 #pragma unroll 2
-      for (int k0 = 0; k0 < C; k0 += 8) {
-        const Frag<true> fk = frag_at<true>(sKp, KP, d0, k0, gid, tig);
+      for (int k0 = 0; k0 < C; k0 += 16) {
+        const FragH fk = frag_at16(sKp, KP, d0, k0, gid, tig);
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const Frag<true> fv = frag_b<true>(sU, SP, k0, n * 8, gid, tig);
-          mma<true>(acc[n], fk, fv);
-        }
+        for (int n = 0; n < 4; ++n) mma16(acc[n], fk, frag_b16(sU, SP, k0, n * 8, gid, tig));
       }
 #pragma unroll
       for (int n = 0; n < 4; ++n)
