@@ -276,7 +276,8 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
         mma16(aq[n], fq, fb);
       }
     }
-    float* intra = p.intra + ci * C * C;
+    // intra as two bf16 planes (hi, lo) in its f32-sized slot
+    uint16_t* intra_h = reinterpret_cast<uint16_t*>(p.intra + ci * C * C);
 #pragma unroll
     for (int n = 0; n < 8; ++n)
 #pragma unroll
@@ -293,21 +294,32 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
           }
           sA[i * AP + j + e] = a[e];
         }
-        *reinterpret_cast<float2*>(intra + i * C + j) = make_float2(q[0], q[1]);
+        uint32_t qh, ql;
+        split_bf16(q[0], q[1], qh, ql);
+        *reinterpret_cast<uint32_t*>(intra_h + i * C + j) = qh;
+        *reinterpret_cast<uint32_t*>(intra_h + C * C + i * C + j) = ql;
       }
   }
   __syncthreads();
   // q' = q e^cum, k' = k e^(last - cum)
   {
-    float* qp = p.qp + ci * C * DK;
-    float* kp = p.kp + ci * C * DK;
+    // as two bf16 planes (hi, lo) each, in their f32-sized slots
+    uint2* qp = reinterpret_cast<uint2*>(p.qp + ci * C * DK);
+    uint2* kp = reinterpret_cast<uint2*>(p.kp + ci * C * DK);
     for (int i = tid; i < C * DK / 4; i += 128) {
       const int r = (i * 4) / DK, d = (i * 4) % DK;
       const float4 q4 = *reinterpret_cast<const float4*>(sQ + r * KP + d);
       const float4 k4 = *reinterpret_cast<const float4*>(sK + r * KP + d);
       const float eq = sEq[r], ek = sEk[r];
-      reinterpret_cast<float4*>(qp)[i] = make_float4(q4.x * eq, q4.y * eq, q4.z * eq, q4.w * eq);
-      reinterpret_cast<float4*>(kp)[i] = make_float4(k4.x * ek, k4.y * ek, k4.z * ek, k4.w * ek);
+      uint2 h, l;
+      split_bf16(q4.x * eq, q4.y * eq, h.x, l.x);
+      split_bf16(q4.z * eq, q4.w * eq, h.y, l.y);
+      qp[i] = h;
+      qp[C * DK / 4 + i] = l;
+      split_bf16(k4.x * ek, k4.y * ek, h.x, l.x);
+      split_bf16(k4.z * ek, k4.w * ek, h.y, l.y);
+      kp[i] = h;
+      kp[C * DK / 4 + i] = l;
     }
   }
   // ---- T = (I + A)^-1 by recursive block inversion, the reference's
@@ -397,75 +409,175 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 #pragma unroll
         for (int n = 0; n < 8; ++n) mma16(acc[n], fa, frag_b16s(src, KP, k0, cb + n * 8, gid, tig, scale));
       }
+      if (is_u) {  // U stays f32: the scan subtracts W S from it at full precision
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const int col = cb + n * 8 + 2 * tig;
-        *reinterpret_cast<float2*>(dst + (r0 + gid) * DK + col) = make_float2(acc[n][0], acc[n][1]);
-        *reinterpret_cast<float2*>(dst + (r0 + gid + 8) * DK + col) = make_float2(acc[n][2], acc[n][3]);
+        for (int n = 0; n < 8; ++n) {
+          const int col = cb + n * 8 + 2 * tig;
+          *reinterpret_cast<float2*>(dst + (r0 + gid) * DK + col) = make_float2(acc[n][0], acc[n][1]);
+          *reinterpret_cast<float2*>(dst + (r0 + gid + 8) * DK + col) = make_float2(acc[n][2], acc[n][3]);
+        }
+      } else {  // W as two bf16 planes (hi, lo)
+        uint16_t* wh = reinterpret_cast<uint16_t*>(dst);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const int col = cb + n * 8 + 2 * tig;
+          uint32_t h, l;
+          split_bf16(acc[n][0], acc[n][1], h, l);
+          *reinterpret_cast<uint32_t*>(wh + (r0 + gid) * DK + col) = h;
+          *reinterpret_cast<uint32_t*>(wh + C * DK + (r0 + gid) * DK + col) = l;
+          split_bf16(acc[n][2], acc[n][3], h, l);
+          *reinterpret_cast<uint32_t*>(wh + (r0 + gid + 8) * DK + col) = h;
+          *reinterpret_cast<uint32_t*>(wh + C * DK + (r0 + gid + 8) * DK + col) = l;
+        }
       }
     }
   }
 }
 
 // ---------------------------------------------------------------------------
+// ldmatrix: four 8 x 8 b16 matrices, row addresses from lanes 8i .. 8i + 7.
+__device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// A split-bf16 operand tile in shared memory: planes hi, lo of [rows][ld].
+struct Planes {
+  uint32_t base;  // shared address of the hi plane
+  int ld;         // elements per row (a multiple of 8)
+  int plane;      // bytes between the hi and the lo plane
+};
+// A (16 x 16) at (r0, k0) of a row-major plane: a0..a3 of m16n8k16.
+__device__ __forceinline__ FragH lda16(const Planes& P, int r0, int k0, int lane) {
+  const int row = r0 + (lane & 7) + ((lane >> 3) & 1) * 8, col = k0 + (lane >> 4) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
+  FragH f;
+  ldm_x4(addr, f.hi);
+  ldm_x4(addr + P.plane, f.lo);
+  return f;
+}
+// A (16 x 16) = the transpose of a row-major plane stored [K][M]: A(m, k) =
+// P[k][m], rows m0 .., k0 ...
+__device__ __forceinline__ FragH lda16_t(const Planes& P, int m0, int k0, int lane) {
+  const int row = k0 + (lane & 7) + (lane >> 4) * 8, col = m0 + ((lane >> 3) & 1) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
+  FragH f;
+  ldm_x4_t(addr, f.hi);
+  ldm_x4_t(addr + P.plane, f.lo);
+  return f;
+}
+// B for two n-blocks (k 16 x n 16) of a plane stored [K][N]: b0, b1 of
+// n0 .. n0 + 7 in hi[0..1] / lo[0..1], of n0 + 8 .. in hi[2..3] / lo[2..3].
+__device__ __forceinline__ FragH ldb16x2(const Planes& P, int k0, int n0, int lane) {
+  const int row = k0 + (lane & 7) + ((lane >> 3) & 1) * 8, col = n0 + (lane >> 4) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
+  FragH f;
+  ldm_x4_t(addr, f.hi);
+  ldm_x4_t(addr + P.plane, f.lo);
+  return f;
+}
+// hi*hi + hi*lo + lo*hi of A with the n-block (0 or 1) of a two-block B.
+__device__ __forceinline__ void mma16b(Acc& acc, const FragH& a, const FragH& b, int nb) {
+  mma_bf16(acc.d, a.hi, b.hi + 2 * nb);
+  mma_bf16(acc.c, a.hi, b.lo + 2 * nb);
+  mma_bf16(acc.e, a.lo, b.hi + 2 * nb);
+}
+
 // 16 warps in two groups of 8; within a group warp w covers rows 16 (w & 3)
 // .. +16 and value columns 16 (w >> 2) .. +16 of the 64 x 32 chunk block.
 //   group 0: W S, then v_new = U - W S, then the state update S = e^last S +
-//            k'^T v_new for state rows 16 w .. +16 (w < dk/16);
+//            k'^T v_new for state rows 16 w .. +16 (w < dk/16), whose f32
+//            values it keeps in registers across chunks;
 //   group 1: q' S, then out = q' S + intra v_new and its store.
-// After v_new is in shared memory the update and the output run side by
-// side, so a chunk's dependent chain is one product shorter on each side.
+// Operands sit in shared memory as split bf16 planes (W, q', k', intra as
+// the prep kernel wrote them; S and v_new split when written) and every
+// fragment is one ldmatrix per plane.  U stays f32.
 constexpr int SCAN_THREADS = 512;
 template <int DK, int DV>
+struct ScanSmem {
+  static constexpr int LK = DK + 8, LS = VS + 8, LC = C + 8;  // bf16 row pitches
+  static constexpr int UP = VS + 8;                           // f32 U row pitch
+  static constexpr int S_B = 2 * DK * LS * 2;                 // S hi/lo
+  static constexpr int M_B = 2 * C * LK * 2;                  // W, q', one k' buffer
+  static constexpr int U_B = C * UP * 4;                      // one U buffer
+  static constexpr int V_B = 2 * C * LS * 2;                  // v_new hi/lo
+  static constexpr int I_B = 2 * C * LC * 2;                  // one intra buffer
+  static constexpr int OFF_S = 0, OFF_W = OFF_S + S_B, OFF_Q = OFF_W + M_B, OFF_K = OFF_Q + M_B;
+  static constexpr int OFF_U = OFF_K + 2 * M_B, OFF_V = OFF_U + 2 * U_B, OFF_I = OFF_V + V_B;
+  static constexpr int BYTES = OFF_I + 2 * I_B;
+  static_assert(BYTES <= 232448, "scan shared memory");
+};
+
+template <int DK, int DV>
 __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
-  constexpr int KP = DK + 4, SP = VS + 8, AP = C + 4;
+  using L = ScanSmem<DK, DV>;
   static_assert(DK % 16 == 0 && DK / 16 <= 8, "16 state rows per warp of group 0");
-  extern __shared__ float sm[];
-  // k', U and intra are double-buffered: chunk ch + 1's copies stream in
-  // while chunk ch computes (W and q' follow once W S and q' S are done).
-  float* sS = sm;                   // [DK][SP]   state slice
-  float* sW = sS + DK * SP;         // [C][KP]
-  float* sQp = sW + C * KP;         // [C][KP]
-  float* sKp0 = sQp + C * KP;       // 2 x [C][KP]
-  float* sU0 = sKp0 + 2 * C * KP;   // 2 x [C][SP]  U slice, then v_new
-  float* sI0 = sU0 + 2 * C * SP;    // 2 x [C][AP]
+  extern __shared__ __align__(16) uint8_t smb[];
+  const uint32_t sb = smem_u32(smb);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int sl = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int c0 = sl * VS;
   const int grp = warp >> 3, w8 = warp & 7;
   const int r0 = (w8 & 3) * 16, n0 = (w8 >> 2) * 16;  // rows / columns of v_new and out
-
-  for (int i = tid; i < DK * VS; i += SCAN_THREADS) {
-    const int d = i / VS, c = i % VS;
-    sS[d * SP + c] = p.s_in ? p.s_in[b * p.s_bs + ((size_t)h * DK + d) * DV + c0 + c] : 0.f;
+  const Planes pS{sb + L::OFF_S, L::LS, DK * L::LS * 2};
+  const Planes pW{sb + L::OFF_W, L::LK, C * L::LK * 2};
+  const Planes pQ{sb + L::OFF_Q, L::LK, C * L::LK * 2};
+  const Planes pV{sb + L::OFF_V, L::LS, C * L::LS * 2};
+  uint16_t* sSh = reinterpret_cast<uint16_t*>(smb + L::OFF_S);
+  uint16_t* sVh = reinterpret_cast<uint16_t*>(smb + L::OFF_V);
+  const bool upd = grp == 0 && warp < DK / 16;
+  const int d0 = warp * 16;  // state rows of an updating warp
+  // An updating warp's 16 state rows x 32 columns, f32, in m16n8 layout.
+  float st[4][4];
+  auto put_s = [&]() {  // the split copy of this warp's state rows
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        uint32_t hi, lo;
+        split_bf16(st[n][2 * hl], st[n][2 * hl + 1], hi, lo);
+        const int o = (d0 + gid + hl * 8) * L::LS + n * 8 + 2 * tig;
+        *reinterpret_cast<uint32_t*>(sSh + o) = hi;
+        *reinterpret_cast<uint32_t*>(sSh + DK * L::LS + o) = lo;
+      }
+  };
+  if (upd) {
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
+        st[n][e] = p.s_in ? p.s_in[b * p.s_bs + ((size_t)h * DK + d) * DV + c0 + c] : 0.f;
+      }
+    put_s();
   }
-  auto load_wq = [&](size_t cj) {
-    const float* w = p.w + cj * C * DK;
-    const float* q = p.qp + cj * C * DK;
-    for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
-      const int r = (i * 4) / DK, d = (i * 4) % DK;
-      cp_async16(sW + r * KP + d, w + 4 * i);
-      cp_async16(sQp + r * KP + d, q + 4 * i);
+  // 16-byte copies of a [2][rows][cols] bf16 slot into planes of pitch ld.
+  auto load_planes = [&](uint8_t* dst, const float* src, int rows, int cols, int ld) {
+    const uint8_t* s8 = reinterpret_cast<const uint8_t*>(src);
+    const int per_row = cols / 8, n = 2 * rows * per_row;
+    for (int i = tid; i < n; i += SCAN_THREADS) {
+      const int pl = i / (rows * per_row), rem = i % (rows * per_row), r = rem / per_row, c8 = rem % per_row;
+      cp_async16(reinterpret_cast<float*>(dst + ((pl * rows + r) * ld + c8 * 8) * 2),
+                 reinterpret_cast<const float*>(s8 + ((size_t)(pl * rows + r) * cols + c8 * 8) * 2));
     }
   };
+  auto load_wq = [&](size_t cj) {
+    load_planes(smb + L::OFF_W, p.w + cj * C * DK, C, DK, L::LK);
+    load_planes(smb + L::OFF_Q, p.qp + cj * C * DK, C, DK, L::LK);
+  };
   auto load_rest = [&](size_t cj, int buf) {
-    const float* k = p.kp + cj * C * DK;
-    float* dk_ = sKp0 + buf * C * KP;
-    for (int i = tid; i < C * DK / 4; i += SCAN_THREADS) {
-      const int r = (i * 4) / DK, d = (i * 4) % DK;
-      cp_async16(dk_ + r * KP + d, k + 4 * i);
-    }
+    load_planes(smb + L::OFF_K + buf * L::M_B, p.kp + cj * C * DK, C, DK, L::LK);
+    load_planes(smb + L::OFF_I + buf * L::I_B, p.intra + cj * C * C, C, C, L::LC);
     const float* u = p.u + cj * C * DV + c0;
-    float* du = sU0 + buf * C * SP;
+    float* du = reinterpret_cast<float*>(smb + L::OFF_U + buf * L::U_B);
     for (int i = tid; i < C * VS / 4; i += SCAN_THREADS) {
       const int r = (i * 4) / VS, c = (i * 4) % VS;
-      cp_async16(du + r * SP + c, u + r * DV + c);
-    }
-    const float* in = p.intra + cj * C * C;
-    float* di = sI0 + buf * C * AP;
-    for (int i = tid; i < C * C / 4; i += SCAN_THREADS) {
-      const int r = (i * 4) / C, c = (i * 4) % C;
-      cp_async16(di + r * AP + c, in + 4 * i);
+      cp_async16(du + r * L::UP + c, u + r * DV + c);
     }
   };
   if (p.n_chunks > 0) {
@@ -475,11 +587,11 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
   for (int ch = 0; ch < p.n_chunks; ++ch) {
     const size_t ci = chunk_index(p, b, ch, h);
     const int buf = ch & 1;
-    float* sKp = sKp0 + buf * C * KP;
-    float* sU = sU0 + buf * C * SP;
-    float* sI = sI0 + buf * C * AP;
+    const Planes pK{sb + L::OFF_K + buf * L::M_B, L::LK, C * L::LK * 2};
+    const Planes pI{sb + L::OFF_I + buf * L::I_B, L::LC, C * L::LC * 2};
+    const float* sU = reinterpret_cast<const float*>(smb + L::OFF_U + buf * L::U_B);
     // This chunk's copies (issued during the previous chunk) have landed,
-    // the previous chunk is done with the other buffers and the state slice
+    // the previous chunk is done with the other buffers and the split state
     // is written.
     cp_async_wait_all();
     __syncthreads();
@@ -487,23 +599,29 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
     const float el = p.elast[ci];
     // group 0: W S; group 1: q' S (over dk)
     Acc acc2[2];
-#pragma unroll
-    for (int n = 0; n < 2; ++n) acc2[n].zero();
-    const float* sA = grp == 0 ? sW : sQp;
+    acc2[0].zero();
+    acc2[1].zero();
+    const Planes& pA = grp == 0 ? pW : pQ;
 #pragma unroll 2
     for (int k0 = 0; k0 < DK; k0 += 16) {
-      const FragH fa = frag_a16(sA, KP, r0, k0, gid, tig);
-#pragma unroll
-      for (int n = 0; n < 2; ++n) mma16(acc2[n], fa, frag_b16(sS, SP, k0, n0 + n * 8, gid, tig));
+      const FragH fa = lda16(pA, r0, k0, lane);
+      const FragH fs = ldb16x2(pS, k0, n0, lane);
+      mma16b(acc2[0], fa, fs, 0);
+      mma16b(acc2[1], fa, fs, 1);
     }
     if (grp == 0) {
-      // v_new = U - W S (in place over U: each warp owns its 16 x 16 block)
+      // v_new = U - W S, split into its planes (each warp owns its 16 x 16 block)
 #pragma unroll
       for (int n = 0; n < 2; ++n)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = r0 + gid + (e >> 1) * 8, j = n0 + n * 8 + 2 * tig + (e & 1);
-          sU[i * SP + j] -= acc2[n].get(e);
+        for (int hl = 0; hl < 2; ++hl) {
+          const int i = r0 + gid + hl * 8, j = n0 + n * 8 + 2 * tig;
+          const float v0 = sU[i * L::UP + j] - acc2[n].get(2 * hl);
+          const float v1 = sU[i * L::UP + j + 1] - acc2[n].get(2 * hl + 1);
+          uint32_t hi, lo;
+          split_bf16(v0, v1, hi, lo);
+          *reinterpret_cast<uint32_t*>(sVh + i * L::LS + j) = hi;
+          *reinterpret_cast<uint32_t*>(sVh + C * L::LS + i * L::LS + j) = lo;
         }
     }
     __syncthreads();
@@ -514,53 +632,55 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
       // out = q' S + intra v_new (intra lower triangular)
 #pragma unroll 1
       for (int k0 = 0; k0 < r0 + 16; k0 += 16) {
-        const FragH fi = frag_a16(sI, AP, r0, k0, gid, tig);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma16(acc2[n], fi, frag_b16(sU, SP, k0, n0 + n * 8, gid, tig));
+        const FragH fi = lda16(pI, r0, k0, lane);
+        const FragH fv = ldb16x2(pV, k0, n0, lane);
+        mma16b(acc2[0], fi, fv, 0);
+        mma16b(acc2[1], fi, fv, 1);
       }
 #pragma unroll
       for (int n = 0; n < 2; ++n)
 #pragma unroll
-        for (int hlf = 0; hlf < 2; ++hlf) {
-          const int t = ch * C + r0 + gid + hlf * 8;
+        for (int hl = 0; hl < 2; ++hl) {
+          const int t = ch * C + r0 + gid + hl * 8;
           if (t < p.T)
             *reinterpret_cast<float2*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + c0 + n0 + n * 8 + 2 * tig) =
-                make_float2(acc2[n].get(2 * hlf), acc2[n].get(2 * hlf + 1));
+                make_float2(acc2[n].get(2 * hl), acc2[n].get(2 * hl + 1));
         }
-    } else if (warp < DK / 16) {
-      // S = e^last S + k'^T v_new: warp w owns state rows 16 w .. 16 w + 15
-      const int d0 = warp * 16;
+    } else if (upd) {
+      // S = e^last S + k'^T v_new on this warp's rows
       Acc acc[4];
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
         acc[n].zero();
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
-          acc[n].d[e] = sS[d * SP + c] * el;
-        }
+        for (int e = 0; e < 4; ++e) acc[n].d[e] = st[n][e] * el;
       }
 #pragma unroll 2
       for (int k0 = 0; k0 < C; k0 += 16) {
-        const FragH fk = frag_at16(sKp, KP, d0, k0, gid, tig);
-#pragma unroll
-        for (int n = 0; n < 4; ++n) mma16(acc[n], fk, frag_b16(sU, SP, k0, n * 8, gid, tig));
+        const FragH fk = lda16_t(pK, d0, k0, lane);
+        const FragH fv0 = ldb16x2(pV, k0, 0, lane), fv1 = ldb16x2(pV, k0, 16, lane);
+        mma16b(acc[0], fk, fv0, 0);
+        mma16b(acc[1], fk, fv0, 1);
+        mma16b(acc[2], fk, fv1, 0);
+        mma16b(acc[3], fk, fv1, 1);
       }
 #pragma unroll
       for (int n = 0; n < 4; ++n)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
-          sS[d * SP + c] = acc[n].get(e);
-        }
+        for (int e = 0; e < 4; ++e) st[n][e] = acc[n].get(e);
+      // the split copy for the next chunk's W S / q' S: nobody reads S
+      // before the next chunk's barrier
+      put_s();
     }
   }
-  __syncthreads();
-  if (p.s_out)
-    for (int i = tid; i < DK * VS; i += SCAN_THREADS) {
-      const int d = i / VS, c = i % VS;
-      p.s_out[(size_t)b * p.nv * DK * DV + ((size_t)h * DK + d) * DV + c0 + c] = sS[d * SP + c];
-    }
+  if (upd && p.s_out)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = d0 + gid + (e >> 1) * 8, c = n * 8 + 2 * tig + (e & 1);
+        p.s_out[(size_t)b * p.nv * DK * DV + ((size_t)h * DK + d) * DV + c0 + c] = st[n][e];
+      }
 }
 
 template <int DK, int DV>
@@ -569,7 +689,7 @@ size_t prep_smem() {
 }
 template <int DK, int DV>
 size_t scan_smem() {
-  return sizeof(float) * (DK * (VS + 8) + 4 * C * (DK + 4) + 2 * C * (VS + 8) + 2 * C * (C + 4));
+  return ScanSmem<DK, DV>::BYTES;
 }
 
 template <int DK, int DV>
