@@ -61,11 +61,6 @@ __device__ __forceinline__ void mma_bf16(float* d, const uint32_t* a, const uint
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
-__device__ __forceinline__ void mma16(Acc& acc, const FragH& a, const FragH& b) {
-  mma_bf16(acc.d, a.hi, b.hi);
-  mma_bf16(acc.c, a.hi, b.lo);
-  mma_bf16(acc.e, a.lo, b.hi);
-}
 // The three products into one register set (the prep kernel's accumulators).
 __device__ __forceinline__ void mma16(float* d, const FragH& a, const FragH& b) {
   mma_bf16(d, a.hi, b.hi);
@@ -85,16 +80,6 @@ __device__ __forceinline__ FragH frag_a16(const float* M, int ld, int r0, int k0
   split_bf16(v3.x, v3.y, f.hi[3], f.lo[3]);
   return f;
 }
-// A (16 x 16) = the transpose of row-major M: A(r, k) = M[k][r].
-__device__ __forceinline__ FragH frag_at16(const float* M, int ld, int r0, int k0, int gid, int tig) {
-  FragH f;
-  const float* p = M + (k0 + 2 * tig) * ld + r0 + gid;
-  split_bf16(p[0], p[ld], f.hi[0], f.lo[0]);
-  split_bf16(p[8], p[ld + 8], f.hi[1], f.lo[1]);
-  split_bf16(p[8 * ld], p[9 * ld], f.hi[2], f.lo[2]);
-  split_bf16(p[8 * ld + 8], p[9 * ld + 8], f.hi[3], f.lo[3]);
-  return f;
-}
 // B (16 x 8) with B(k, n) = M[k][n] (row-major [K][N]).
 __device__ __forceinline__ FragH frag_b16(const float* M, int ld, int k0, int n0, int gid, int tig) {
   FragH f;
@@ -103,22 +88,90 @@ __device__ __forceinline__ FragH frag_b16(const float* M, int ld, int k0, int n0
   split_bf16(p[8 * ld], p[9 * ld], f.hi[1], f.lo[1]);
   return f;
 }
-// B (16 x 8) with B(k, n) = M[k][n] * s[k].
-__device__ __forceinline__ FragH frag_b16s(const float* M, int ld, int k0, int n0, int gid, int tig, const float* s) {
+
+// ---------------------------------------------------------------------------
+// ldmatrix: four 8 x 8 b16 matrices, row addresses from lanes 8i .. 8i + 7.
+__device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// A split-bf16 operand tile in shared memory: planes hi, lo of [rows][ld].
+struct Planes {
+  uint32_t base;  // shared address of the hi plane
+  int ld;         // elements per row (a multiple of 8)
+  int plane;      // bytes between the hi and the lo plane
+};
+// A (16 x 16) at (r0, k0) of a row-major plane: a0..a3 of m16n8k16.
+__device__ __forceinline__ FragH lda16(const Planes& P, int r0, int k0, int lane) {
+  const int row = r0 + (lane & 7) + ((lane >> 3) & 1) * 8, col = k0 + (lane >> 4) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
   FragH f;
-  const int k = k0 + 2 * tig;
-  const float* p = M + k * ld + n0 + gid;
-  split_bf16(p[0] * s[k], p[ld] * s[k + 1], f.hi[0], f.lo[0]);
-  split_bf16(p[8 * ld] * s[k + 8], p[9 * ld] * s[k + 9], f.hi[1], f.lo[1]);
+  ldm_x4(addr, f.hi);
+  ldm_x4(addr + P.plane, f.lo);
   return f;
 }
-// B (16 x 8) with B(k, n) = M[n][k] (B = M^T, M row-major [N][K]).
-__device__ __forceinline__ FragH frag_bt16(const float* M, int ld, int k0, int n0, int gid, int tig) {
+// A (16 x 16) = the transpose of a row-major plane stored [K][M]: A(m, k) =
+// P[k][m], rows m0 .., k0 ...
+__device__ __forceinline__ FragH lda16_t(const Planes& P, int m0, int k0, int lane) {
+  const int row = k0 + (lane & 7) + (lane >> 4) * 8, col = m0 + ((lane >> 3) & 1) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
   FragH f;
-  const float* p = M + (n0 + gid) * ld + k0 + 2 * tig;
-  const float2 v0 = *reinterpret_cast<const float2*>(p), v1 = *reinterpret_cast<const float2*>(p + 8);
-  split_bf16(v0.x, v0.y, f.hi[0], f.lo[0]);
-  split_bf16(v1.x, v1.y, f.hi[1], f.lo[1]);
+  ldm_x4_t(addr, f.hi);
+  ldm_x4_t(addr + P.plane, f.lo);
+  return f;
+}
+// B for two n-blocks (k 16 x n 16) of a plane stored [K][N]: b0, b1 of
+// n0 .. n0 + 7 in hi[0..1] / lo[0..1], of n0 + 8 .. in hi[2..3] / lo[2..3].
+__device__ __forceinline__ FragH ldb16x2(const Planes& P, int k0, int n0, int lane) {
+  const int row = k0 + (lane & 7) + ((lane >> 3) & 1) * 8, col = n0 + (lane >> 4) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
+  FragH f;
+  ldm_x4_t(addr, f.hi);
+  ldm_x4_t(addr + P.plane, f.lo);
+  return f;
+}
+// hi*hi + hi*lo + lo*hi of A with the n-block (0 or 1) of a two-block B.
+__device__ __forceinline__ void mma16b(Acc& acc, const FragH& a, const FragH& b, int nb) {
+  mma_bf16(acc.d, a.hi, b.hi + 2 * nb);
+  mma_bf16(acc.c, a.hi, b.lo + 2 * nb);
+  mma_bf16(acc.e, a.lo, b.hi + 2 * nb);
+}
+
+// B for two n-blocks (k 16 x n 16) of a plane stored [N][K] (B = P^T):
+// B(k, n) = P[n][k], n-blocks n0 .. n0 + 7 and n0 + 8 .. n0 + 15.
+__device__ __forceinline__ FragH ldb16x2_nt(const Planes& P, int n0, int k0, int lane) {
+  const int row = n0 + (lane & 7) + (lane >> 4) * 8, col = k0 + ((lane >> 3) & 1) * 8;
+  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
+  FragH f;
+  ldm_x4(addr, f.hi);
+  ldm_x4(addr + P.plane, f.lo);
+  return f;
+}
+// The three products of A with n-block nb of a two-block B into one
+// register set.
+__device__ __forceinline__ void mma16n(float* d, const FragH& a, const FragH& b, int nb) {
+  mma_bf16(d, a.hi, b.hi + 2 * nb);
+  mma_bf16(d, a.hi, b.lo + 2 * nb);
+  mma_bf16(d, a.lo, b.hi + 2 * nb);
+}
+// A (16 x 16) from f32 row-major M at (r0, k0) with column scale: A(r, k) =
+// M[r][k] * s[k].
+__device__ __forceinline__ FragH frag_a16s(const float* M, int ld, int r0, int k0, int gid, int tig, const float* s) {
+  FragH f;
+  const int k = k0 + 2 * tig;
+  const float* p0 = M + (r0 + gid) * ld + k;
+  const float* p1 = p0 + 8 * ld;
+  const float s0 = s[k], s1 = s[k + 1], s8 = s[k + 8], s9 = s[k + 9];
+  split_bf16(p0[0] * s0, p0[1] * s1, f.hi[0], f.lo[0]);
+  split_bf16(p1[0] * s0, p1[1] * s1, f.hi[1], f.lo[1]);
+  split_bf16(p0[8] * s8, p0[9] * s9, f.hi[2], f.lo[2]);
+  split_bf16(p1[8] * s8, p1[9] * s9, f.hi[3], f.lo[3]);
   return f;
 }
 
@@ -155,12 +208,14 @@ __host__ __device__ inline size_t chunk_index(const Params& p, int b, int ch, in
 template <int DK, int DV>
 __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
   static_assert(DK == DV, "v is staged in the q buffer");
-  constexpr int KP = DK + 4, AP = C + 4;
+  constexpr int LK = DK + 8, AP = C + 4;
   constexpr int NL = C * (DK / 8) / 128;  // 16-byte loads per thread per matrix
-  extern __shared__ float sm[];
-  float* sQ = sm;             // [C][KP]  q, then v
-  float* sK = sQ + C * KP;    // [C][KP]
-  float* sA = sK + C * KP;    // [C][AP]  A (strict lower)
+  extern __shared__ __align__(16) float sm[];
+  // q (then v) and k as split bf16 planes [2][C][LK] (hi, lo), each in the
+  // bytes of an f32 [C][LK] tile; every product fragment is an ldmatrix.
+  uint16_t* sQh = reinterpret_cast<uint16_t*>(sm);
+  uint16_t* sKh = sQh + 2 * C * LK;
+  float* sA = sm + 2 * C * LK;  // [C][AP]  A (strict lower)
   float* sT = sA + C * AP;    // [C][AP]  T = (I + A)^-1
   float* sG = sT + C * AP;    // cum
   float* sB = sG + C;         // beta
@@ -174,6 +229,17 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
   const int t0 = ch * C;
   const int key_dim = p.nk * DK;
   const size_t ci = chunk_index(p, b, ch, h);
+  const Planes pQ{smem_u32(sQh), LK, C * LK * 2};
+  const Planes pK{smem_u32(sKh), LK, C * LK * 2};
+  auto store_split8 = [&](uint16_t* P, int r, int c8, const float* f, float sc) {
+    uint4 hv, lv;
+    split_bf16(f[0] * sc, f[1] * sc, hv.x, lv.x);
+    split_bf16(f[2] * sc, f[3] * sc, hv.y, lv.y);
+    split_bf16(f[4] * sc, f[5] * sc, hv.z, lv.z);
+    split_bf16(f[6] * sc, f[7] * sc, hv.w, lv.w);
+    *reinterpret_cast<uint4*>(P + r * LK + c8) = hv;
+    *reinterpret_cast<uint4*>(P + C * LK + r * LK + c8) = lv;
+  };
 
   // ---- all q, k, v loads in flight at once (bf16), zero past T ----
   uint4 qv[NL], kv[NL], vv[NL];
@@ -206,10 +272,6 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 #pragma unroll
     for (int x = 0; x < 8; ++x) f[x] = __bfloat162float(e[x]);
   };
-  auto store8 = [](float* dst, const float* f, float sc) {
-    reinterpret_cast<float4*>(dst)[0] = make_float4(f[0] * sc, f[1] * sc, f[2] * sc, f[3] * sc);
-    reinterpret_cast<float4*>(dst)[1] = make_float4(f[4] * sc, f[5] * sc, f[6] * sc, f[7] * sc);
-  };
   // l2norm of the q and k rows from registers (q also * dk^-1/2): the DK/8
   // threads of a row are consecutive lanes, reduced with shuffles.
   const float qscale = rsqrtf((float)DK);
@@ -230,8 +292,8 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
       sq += __shfl_xor_sync(0xffffffffu, sq, o);
       sk += __shfl_xor_sync(0xffffffffu, sk, o);
     }
-    store8(sQ + r * KP + c8, fq, (1.f / sqrtf(sq + 1e-6f)) * qscale);
-    store8(sK + r * KP + c8, fk, 1.f / sqrtf(sk + 1e-6f));
+    store_split8(sQh, r, c8, fq, (1.f / sqrtf(sq + 1e-6f)) * qscale);
+    store_split8(sKh, r, c8, fk, 1.f / sqrtf(sk + 1e-6f));
   }
   __syncthreads();
   // ---- cumsum of g over the chunk: warp 0, two tokens a lane, lane scan ----
@@ -266,14 +328,18 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
       for (int e = 0; e < 4; ++e) ak[n][e] = aq[n][e] = 0.f;
 #pragma unroll 1
     for (int k0 = 0; k0 < DK; k0 += 16) {
-      const FragH fk = frag_a16(sK, KP, r0, k0, gid, tig);
-      const FragH fq = frag_a16(sQ, KP, r0, k0, gid, tig);
+      const FragH fk = lda16(pK, r0, k0, lane);
+      const FragH fq = lda16(pQ, r0, k0, lane);
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < 8; n += 2) {
         if (n * 8 > r0 + 15) continue;  // strictly above the diagonal block
-        const FragH fb = frag_bt16(sK, KP, k0, n * 8, gid, tig);
-        mma16(ak[n], fk, fb);
-        mma16(aq[n], fq, fb);
+        const FragH fb = ldb16x2_nt(pK, n * 8, k0, lane);  // k^T for column blocks n, n + 1
+        mma16n(ak[n], fk, fb, 0);
+        mma16n(aq[n], fq, fb, 0);
+        if ((n + 1) * 8 <= r0 + 15) {
+          mma16n(ak[n + 1], fk, fb, 1);
+          mma16n(aq[n + 1], fq, fb, 1);
+        }
       }
     }
     // intra as two bf16 planes (hi, lo) in its f32-sized slot
@@ -308,8 +374,16 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
     uint2* kp = reinterpret_cast<uint2*>(p.kp + ci * C * DK);
     for (int i = tid; i < C * DK / 4; i += 128) {
       const int r = (i * 4) / DK, d = (i * 4) % DK;
-      const float4 q4 = *reinterpret_cast<const float4*>(sQ + r * KP + d);
-      const float4 k4 = *reinterpret_cast<const float4*>(sK + r * KP + d);
+      // q, k = hi + lo from the planes
+      auto rd4 = [&](const uint16_t* P) {
+        const uint2 hv = *reinterpret_cast<const uint2*>(P + r * LK + d);
+        const uint2 lv = *reinterpret_cast<const uint2*>(P + C * LK + r * LK + d);
+        return make_float4(__uint_as_float(hv.x << 16) + __uint_as_float(lv.x << 16),
+                           __uint_as_float(hv.x & 0xffff0000u) + __uint_as_float(lv.x & 0xffff0000u),
+                           __uint_as_float(hv.y << 16) + __uint_as_float(lv.y << 16),
+                           __uint_as_float(hv.y & 0xffff0000u) + __uint_as_float(lv.y & 0xffff0000u));
+      };
+      const float4 q4 = rd4(sQh), k4 = rd4(sKh);
       const float eq = sEq[r], ek = sEk[r];
       uint2 h, l;
       split_bf16(q4.x * eq, q4.y * eq, h.x, l.x);
@@ -382,9 +456,9 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
 #pragma unroll
   for (int u = 0; u < NL; ++u) {
     const int i = tid + u * 128, r = i / (DK / 8), c8 = (i % (DK / 8)) * 8;
-    float fv[8];
-    unpack8(vv[u], fv);
-    store8(sQ + r * KP + c8, fv, 1.f);
+    // v is exact in bf16: hi = v, lo = 0
+    *reinterpret_cast<uint4*>(sQh + r * LK + c8) = vv[u];
+    *reinterpret_cast<uint4*>(sQh + C * LK + r * LK + c8) = make_uint4(0, 0, 0, 0);
   }
   __syncthreads();
   // ---- W = T (k beta e^cum), U = T (v beta) (T lower triangular) ----
@@ -395,7 +469,9 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
     for (int part = 0; part < 2 * (DK / 64); ++part) {  // 64 output columns of W, then of U
       const bool is_u = part >= DK / 64;
       const int cb = (part % (DK / 64)) * 64;
-      const float* src = is_u ? sQ : sK;
+      // W = T diag(beta e^cum) k, U = T diag(beta) v: the row scales of k / v
+      // go onto T's columns so that k and v feed the MMAs by ldmatrix
+      const Planes& pB = is_u ? pQ : pK;
       const float* scale = is_u ? sB : sSw;
       float* dst = (is_u ? p.u : p.w) + ci * C * DK;
       float acc[8][4];
@@ -405,9 +481,13 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
         for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
 #pragma unroll 1
       for (int k0 = 0; k0 < kend; k0 += 16) {
-        const FragH fa = frag_a16(sT, AP, r0, k0, gid, tig);
+        const FragH fa = frag_a16s(sT, AP, r0, k0, gid, tig, scale);
 #pragma unroll
-        for (int n = 0; n < 8; ++n) mma16(acc[n], fa, frag_b16s(src, KP, k0, cb + n * 8, gid, tig, scale));
+        for (int n = 0; n < 8; n += 2) {
+          const FragH fb = ldb16x2(pB, k0, cb + n * 8, lane);
+          mma16n(acc[n], fa, fb, 0);
+          mma16n(acc[n + 1], fa, fb, 1);
+        }
       }
       if (is_u) {  // U stays f32: the scan subtracts W S from it at full precision
 #pragma unroll
@@ -432,60 +512,6 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
       }
     }
   }
-}
-
-// ---------------------------------------------------------------------------
-// ldmatrix: four 8 x 8 b16 matrices, row addresses from lanes 8i .. 8i + 7.
-__device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldm_x4_t(uint32_t addr, uint32_t* r) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-// A split-bf16 operand tile in shared memory: planes hi, lo of [rows][ld].
-struct Planes {
-  uint32_t base;  // shared address of the hi plane
-  int ld;         // elements per row (a multiple of 8)
-  int plane;      // bytes between the hi and the lo plane
-};
-// A (16 x 16) at (r0, k0) of a row-major plane: a0..a3 of m16n8k16.
-__device__ __forceinline__ FragH lda16(const Planes& P, int r0, int k0, int lane) {
-  const int row = r0 + (lane & 7) + ((lane >> 3) & 1) * 8, col = k0 + (lane >> 4) * 8;
-  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
-  FragH f;
-  ldm_x4(addr, f.hi);
-  ldm_x4(addr + P.plane, f.lo);
-  return f;
-}
-// A (16 x 16) = the transpose of a row-major plane stored [K][M]: A(m, k) =
-// P[k][m], rows m0 .., k0 ...
-__device__ __forceinline__ FragH lda16_t(const Planes& P, int m0, int k0, int lane) {
-  const int row = k0 + (lane & 7) + (lane >> 4) * 8, col = m0 + ((lane >> 3) & 1) * 8;
-  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
-  FragH f;
-  ldm_x4_t(addr, f.hi);
-  ldm_x4_t(addr + P.plane, f.lo);
-  return f;
-}
-// B for two n-blocks (k 16 x n 16) of a plane stored [K][N]: b0, b1 of
-// n0 .. n0 + 7 in hi[0..1] / lo[0..1], of n0 + 8 .. in hi[2..3] / lo[2..3].
-__device__ __forceinline__ FragH ldb16x2(const Planes& P, int k0, int n0, int lane) {
-  const int row = k0 + (lane & 7) + ((lane >> 3) & 1) * 8, col = n0 + (lane >> 4) * 8;
-  const uint32_t addr = P.base + (uint32_t)(row * P.ld + col) * 2;
-  FragH f;
-  ldm_x4_t(addr, f.hi);
-  ldm_x4_t(addr + P.plane, f.lo);
-  return f;
-}
-// hi*hi + hi*lo + lo*hi of A with the n-block (0 or 1) of a two-block B.
-__device__ __forceinline__ void mma16b(Acc& acc, const FragH& a, const FragH& b, int nb) {
-  mma_bf16(acc.d, a.hi, b.hi + 2 * nb);
-  mma_bf16(acc.c, a.hi, b.lo + 2 * nb);
-  mma_bf16(acc.e, a.lo, b.hi + 2 * nb);
 }
 
 // 16 warps in two groups of 8; within a group warp w covers rows 16 (w & 3)
@@ -685,7 +711,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) gdn_scan_kernel(Params p) {
 
 template <int DK, int DV>
 size_t prep_smem() {
-  return sizeof(float) * (2 * C * (DK + 4) + 2 * C * (C + 4) + 5 * C + 32 * 36);
+  return sizeof(float) * (2 * C * (DK + 8) + 2 * C * (C + 4) + 5 * C + 32 * 36);
 }
 template <int DK, int DV>
 size_t scan_smem() {
