@@ -604,22 +604,19 @@ static int launch_tc(const void* q, const void* k, const void* v, void* const* o
 }
 
 int attn_tc_launch(const void* q, const void* k, const void* v, void* const* o, int n_o, int n_tokens, int n_kv_rows,
-                   int hq, int hkv,
-                   int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs, int n_tiles, float scale,
-                   int n_split, void* workspace, cudaStream_t stream) {
+                   int hq, int hkv, int D, int q_rs, int kv_rs, int o_rs, const cevk_segment* segs, int n_segs,
+                   int n_tiles, float scale, int n_split, void* workspace, cudaStream_t stream) {
+  // head_dim 64 / 128: two CTAs per SM; 256: one (its O takes 256 TMEM columns)
+#define CEVK_ATTN(DD, KSK, KSV)                                                                                    \
+  return launch_tc<DD, 64, KSK, KSV, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, \
+                                        n_segs, n_tiles, scale, n_split, workspace, stream)
   switch (D) {
-    case 64:
-      return launch_tc<64, 64, 6, 4, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                     scale, n_split, workspace, stream);
-    case 128:
-      return launch_tc<128, 64, 3, 2, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                      scale, n_split, workspace, stream);
-    case 256:
-      return launch_tc<256, 64, 3, 2, 1>(q, k, v, o, n_o, n_tokens, n_kv_rows, hq, hkv, q_rs, kv_rs, o_rs, segs, n_segs, n_tiles,
-                                      scale, n_split, workspace, stream);
-    default:
-      return set_error(CEVK_E_SHAPE, "bf16 attention supports head_dim 64, 128, 256 (got %d)", D);
+    case 64: CEVK_ATTN(64, 6, 4);
+    case 128: CEVK_ATTN(128, 3, 2);
+    case 256: CEVK_ATTN(256, 3, 2);
+    default: return set_error(CEVK_E_SHAPE, "bf16 attention supports head_dim 64, 128, 256 (got %d)", D);
   }
+#undef CEVK_ATTN
 }
 
 }  // namespace cevk
