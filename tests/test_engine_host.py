@@ -1,0 +1,84 @@
+"""Host-side scheduling of the packed engine without a GPU: the joint
+chunked prefill of several requests' prefix heads (one pass per chunk
+index, at most pass_tokens tokens, one segment per head seeing its own
+earlier chunks fully and itself causally) and the packed-pass layout."""
+from types import SimpleNamespace
+
+from cev_b200.engine import Engine
+
+
+class _Recorder:
+    def __init__(self):
+        self.calls = []
+
+    def run_tokens(self, tokens, pos, rows, segs):
+        self.calls.append((list(tokens), list(pos), list(rows), [tuple(s) for s in segs]))
+
+
+def _engine(chunk, pass_tokens):
+    eng = Engine.__new__(Engine)  # host logic only: no model weights
+    eng.model = _Recorder()
+    eng.prefill_chunk = chunk
+    eng.pass_tokens = pass_tokens
+    return eng
+
+
+def _plan(start):
+    return SimpleNamespace(kv=SimpleNamespace(start=start))
+
+
+def test_joint_prefill_packs_chunk_c_of_every_head():
+    eng = _engine(4, 16)
+    a, b = _plan(100), _plan(300)
+    eng._prefill_heads([(a, list(range(10))), (b, list(range(50, 56)))])
+    calls = eng.model.calls
+    assert len(calls) == 3  # chunk indices 0, 1, 2 (head a has 3 chunks, b has 2)
+    toks, pos, rows, segs = calls[0]
+    assert toks == [0, 1, 2, 3, 50, 51, 52, 53]
+    assert pos == [0, 1, 2, 3, 0, 1, 2, 3]
+    assert rows == [100, 101, 102, 103, 300, 301, 302, 303]
+    assert segs == [(0, 4, 100, 0, 100), (4, 4, 300, 0, 300)]
+    toks, pos, rows, segs = calls[1]
+    assert toks == [4, 5, 6, 7, 54, 55] and pos == [4, 5, 6, 7, 4, 5]
+    assert segs == [(0, 4, 100, 4, 104), (4, 2, 300, 4, 304)]  # each sees its own 4 earlier rows
+    assert calls[2] == ([8, 9], [8, 9], [108, 109], [(0, 2, 100, 8, 108)])
+
+
+def test_joint_prefill_splits_a_chunk_index_at_pass_tokens():
+    eng = _engine(4, 6)  # room for one 4-token part per pass (cap = max(6, 4))
+    heads = [(_plan(0), list(range(8))), (_plan(50), list(range(8))), (_plan(90), list(range(3)))]
+    eng._prefill_heads(heads)
+    sizes = [len(c[0]) for c in eng.model.calls]
+    assert sizes == [4, 4, 3, 4, 4]  # chunk 0: 4 | 4 | 3 (4 + 3 > 6); chunk 1: 4 | 4
+    # every token of every head is prefilled exactly once, at its position
+    seen = {}
+    for toks, pos, rows, segs in eng.model.calls:
+        for q0, n, po, pl, so in segs:
+            assert pl == pos[q0] and so == po + pl  # own rows follow the head's earlier rows
+            for i in range(n):
+                seen[(po, pos[q0 + i])] = rows[q0 + i]
+    assert len(seen) == 8 + 8 + 3
+    assert all(row == start + p for (start, p), row in seen.items())
+
+
+def test_joint_prefill_of_nothing_runs_nothing():
+    eng = _engine(512, 2048)
+    eng._prefill_heads([])
+    assert eng.model.calls == []
+
+
+def test_pass_layout_tails_then_suffixes():
+    """engine.rs:389-442 without the mask: pending tails first (absolute
+    positions, written into their prefix rows, seeing the head fully), then
+    each suffix (positions from the prefix end, scratch rows, seeing the
+    whole prefix), with one readout row per suffix at its last token."""
+    a = SimpleNamespace(prefix=[1, 2, 3, 4, 5], head=3, tail=range(3, 5), kv=SimpleNamespace(start=40),
+                        suffixes=[[7, 8], [9]])
+    b = SimpleNamespace(prefix=[6, 6], head=2, tail=range(2, 2), kv=SimpleNamespace(start=10),
+                        suffixes=[[5, 5, 5]])
+    tokens, pos, rows, segs, gather, n_scratch = Engine.pass_layout([a, b], [(0, 1), (1, 0), (0, 0)], 1000)
+    assert tokens == [4, 5, 9, 5, 5, 5, 7, 8]
+    assert pos == [3, 4, 5, 2, 3, 4, 5, 6]
+    assert rows == [43, 44, 1000, 1001, 1002, 1003, 1004, 1005]
+    assert segs == [(0, 2, 40, 3, 43), (2, 1, 40, 5, 1000), (3, 3, 10, 2, 1001), (6, 2, 40, 5, 1004)]
+    assert gather == [2, 5, 7] and n_scratch == 6
