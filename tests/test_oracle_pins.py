@@ -2,7 +2,7 @@
 
 These restate, with the same deterministic inputs and tolerances, the unit
 tests the reference ships for this path, so the oracle's arithmetic is pinned
-to the reference's before it is used to judge the GPU library.
+to the reference's before it is used to check the GPU library.
 """
 import math
 
