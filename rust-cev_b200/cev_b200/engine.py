@@ -143,6 +143,9 @@ class Engine:
                     n += 1
                 batch, rest = rest[:n], rest[n:]
                 self._pass(plans, batch, readouts)
+            # a bounded device wait that gave up fails the call instead of
+            # serving its rows
+            ops.device_status()
             return [Output(r, len(p.prefix) + sum(len(s) for s in p.suffixes), p.cached)
                     for p, r in zip(plans, readouts)]
         finally:

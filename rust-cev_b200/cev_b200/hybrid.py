@@ -353,6 +353,9 @@ class HybridEngine:
             state.pins -= 1
             if not cached and not self.cache.put(list(req.prefix), state) and not state.pins:
                 state.release()
+        # a bounded device wait that gave up (an attention pipeline, a peer's
+        # head rows) fails the request instead of serving its rows
+        ops.device_status()
         return Output(readouts, len(req.prefix) + sum(len(s) for s in req.suffixes), cached)
 
     def run_many(self, reqs):
