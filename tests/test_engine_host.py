@@ -82,3 +82,87 @@ def test_pass_layout_tails_then_suffixes():
     assert rows == [43, 44, 1000, 1001, 1002, 1003, 1004, 1005]
     assert segs == [(0, 2, 40, 3, 43), (2, 1, 40, 5, 1000), (3, 3, 10, 2, 1001), (6, 2, 40, 5, 1004)]
     assert gather == [2, 5, 7] and n_scratch == 6
+
+
+# ---- planning, the prefix cache and the arena rows (engine.rs:327-363, 474-503) ----
+import pytest  # noqa: E402
+import torch  # noqa: E402
+
+from cev_b200.arena import KvArena, PrefixCache, RowAllocator  # noqa: E402
+from cev_b200.engine import InputError, Request  # noqa: E402
+from cev_b200.qwen3 import PrefixKv  # noqa: E402
+
+
+def _planning_engine(max_len=128, rows=1024, budget=65536):
+    eng = Engine.__new__(Engine)
+    eng.model = SimpleNamespace(max_len=max_len, arena=KvArena(1, rows, 1, 8, torch.float32, "cpu"))
+    eng.cache = PrefixCache(budget)
+    eng.prefill_chunk, eng.pass_tokens = 16, 64
+    return eng
+
+
+def test_plan_rejects_a_prompt_at_the_context_limit():
+    """engine.rs:350-352 on the joint token ids: the longest full prompt
+    must stay below max_len (the check_fits slack of engine.rs:513-524 is a
+    pre-tokenisation shortcut; token ids here are exact)."""
+    eng = _planning_engine(max_len=128)
+    p = eng._plan(Request([1] * 100, [[2] * 20, [3] * 27], [1, 1]))
+    assert not p.cached and p.kv.capacity == 100
+    with pytest.raises(InputError, match="context limit is 128"):
+        eng._plan(Request([1] * 100, [[2] * 20, [3] * 28], [1, 1]))
+    with pytest.raises(InputError, match="context limit"):
+        eng._plan(Request([1] * 128, [[2]], [1]))
+    with pytest.raises(InputError, match="empty shared prefix"):
+        eng._plan(Request([], [[2]], [1]))
+
+
+def test_plan_reuses_and_pins_a_cached_prefix():
+    eng = _planning_engine()
+    arena = eng.model.arena
+    kv = PrefixKv(arena, arena.alloc(40), 40, 40)
+    assert eng.cache.put([5] * 40, kv)
+    p = eng._plan(Request([5] * 40, [[1, 2]], [1]))
+    assert p.cached and p.kv is kv and kv.pins == 1 and p.head == 40 and len(p.tail) == 0
+    q = eng._plan(Request([6] * 40, [[1, 2]], [1]))
+    assert not q.cached and q.kv.start != kv.start  # a new range; the cached rows stay
+
+
+def test_prefix_cache_evicts_least_recent_unpinned_and_frees_rows():
+    arena = KvArena(1, 300, 1, 4, torch.float32, "cpu")
+    cache = PrefixCache(budget=250)
+    states = []
+    for i in range(3):
+        st = PrefixKv(arena, arena.alloc(100), 100, 100)
+        states.append(st)
+        assert cache.put([i] * 100, st)
+    # 300 cached tokens > 250: the oldest (key 0) went, its rows are free
+    assert states[0].released and cache.peek([0] * 100) is None
+    assert arena.rows.used() == 200
+    states[1].pins = 1  # a running request reads key 1
+    cache.get([2] * 100)  # key 2 is now the most recent
+    assert cache.evict_one() and states[2].released and not states[1].released
+    assert not cache.evict_one()  # only the pinned entry is left
+    assert cache.put([9] * 300, PrefixKv(arena, 0, 300, 300)) is False  # over budget alone: not cached
+
+
+def test_arena_evicts_cache_entries_when_full():
+    arena = KvArena(1, 200, 1, 4, torch.float32, "cpu")
+    cache = PrefixCache(budget=10_000)
+    a = PrefixKv(arena, arena.alloc(150), 150, 150)
+    cache.put([1] * 150, a)
+    start = arena.alloc(120, cache)  # needs a's rows: a is evicted
+    assert a.released and start == 0
+    with pytest.raises(MemoryError):
+        arena.alloc(100, cache)  # 80 free, nothing left to evict
+
+
+def test_row_allocator_first_fit_and_merging():
+    r = RowAllocator(100)
+    a, b, c = r.alloc(30), r.alloc(30), r.alloc(30)
+    assert (a, b, c) == (0, 30, 60) and r.alloc(20) is None
+    r.release(b, 30)
+    assert r.alloc(40) is None and r.alloc(25) == 30  # first fit into the hole
+    r.release(30, 25)
+    r.release(a, 30)
+    r.release(c, 30)
+    assert r.free == [(0, 100)] and r.used() == 0  # neighbours merged back
