@@ -166,3 +166,48 @@ def test_row_allocator_first_fit_and_merging():
     r.release(a, 30)
     r.release(c, 30)
     assert r.free == [(0, 100)] and r.used() == 0  # neighbours merged back
+
+
+# ---- the hybrid engine's state prefill and padded rows (hybrid.rs:555-617) ----
+class _RecordingDecoder:
+    def __init__(self):
+        self.calls = []
+
+    def new_state(self, n, cache):
+        return SimpleNamespace(pins=0, released=False, next_pos=0, release=lambda: None)
+
+    def forward(self, ids, B, T, pos, state, keep, cache):
+        self.calls.append((list(ids), B, T, list(pos), keep))
+        if keep:
+            state.next_pos = max(pos) + 1
+        return "x"
+
+
+def _hybrid(chunk):
+    from cev_b200.hybrid import HybridEngine
+    eng = HybridEngine.__new__(HybridEngine)  # host logic only
+    eng.decoder = _RecordingDecoder()
+    eng.pad_id = 0
+    eng.prefill_chunk = chunk
+    eng.pass_tokens = 64
+    eng.cache = PrefixCache(1000)
+    return eng
+
+
+def test_hybrid_prefill_runs_the_state_in_chunks_and_pins_it():
+    eng = _hybrid(512)
+    st = eng.prefill(list(range(1, 1101)))
+    calls = eng.decoder.calls
+    assert [(c[1], c[2]) for c in calls] == [(1, 512), (1, 512), (1, 76)]
+    assert [c[3][0] for c in calls] == [0, 512, 1024] and calls[-1][3][-1] == 1099
+    assert all(c[4] for c in calls) and st.pins == 1 and st.next_pos == 1100
+
+
+def test_hybrid_rows_are_right_padded_and_continue_the_state():
+    eng = _hybrid(512)
+    state = SimpleNamespace(next_pos=300)
+    x, t = eng.rows(state, [[5, 6, 7], [8, 9, 10, 11, 12], [13]])
+    ids, B, T, pos, keep = eng.decoder.calls[0]
+    assert (x, t, B, T, keep) == ("x", 5, 3, 5, False)
+    assert ids == [5, 6, 7, 0, 0, 8, 9, 10, 11, 12, 13, 0, 0, 0, 0]
+    assert pos == [300, 301, 302, 303, 304]  # every row continues at the state's next position
