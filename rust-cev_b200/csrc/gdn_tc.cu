@@ -17,9 +17,11 @@
 //   A = strict_lower(beta_i k_i.k_j e^(cum_i - cum_j)), T = (I + A)^-1 by
 //   recursive block inversion; intra = lower(q_i.k_j e^(cum_i - cum_j));
 //   W = T (k beta e^cum), U = T (v beta), q' = q e^cum, k' = k e^(last - cum).
-//   All of it to the workspace (f32).
+//   All of it to the workspace: W, q', k' and intra as split bf16 planes
+//   (hi, lo) in their f32-sized slots, U and e^last in f32.
 // gdn_scan_kernel -- one CTA per (value head, 32 value columns, row), over
-//   the chunks in order, state slice S (dk x 32) in shared memory:
+//   the chunks in order, state slice S (dk x 32) in registers of its
+//   update warps, with a split bf16 copy in shared memory for the products:
 //   v_new = U - W S;  out = q' S + intra v_new;  S = e^last S + k'^T v_new.
 // The raw output goes to the workspace's core array; gdn.cu's gated-norm
 // kernel finishes y.
@@ -203,7 +205,7 @@ __host__ __device__ inline size_t chunk_index(const Params& p, int b, int ch, in
 }
 
 // ---------------------------------------------------------------------------
-// 103.7 KB of shared memory (dk = dv = 128): two CTAs per SM.  v reuses the
+// 107.8 KB of shared memory (dk = dv = 128): two CTAs per SM.  v reuses the
 // q buffer once q' is written.
 template <int DK, int DV>
 __global__ void __launch_bounds__(128, 2) gdn_prep_kernel(Params p) {
