@@ -5,8 +5,10 @@
 // (qwen3.rs:190-200, qwen35.rs:529-541, lfm2.rs:147-156).
 //
 // One block per token (cos/sin computed once per token), one warp per head
-// row; the warp holds the row in shared memory so the rotation partner
-// (d +- rot/2) can live in any lane.  HBM-bound: each element is read once
+// row.  For head_dim 64 / 128 / 256 (qk_norm_rope_vec_kernel) a lane holds
+// D/32 consecutive elements and takes the rotation partner (d +- rot/2) from
+// another lane by shuffle; other shapes go through a shared-memory row so
+// the partner can live in any lane.  HBM-bound: each element is read once
 // and written once.
 #include <cmath>
 #include <type_traits>
