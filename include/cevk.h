@@ -292,7 +292,9 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
  *     split them or use the workspace entry point.
  *   - The first call on a device looks up the array's device address (once
  *     per device, with that device current); make that first call before
- *     any stream capture.
+ *     any stream capture.  The address is kept for the life of the process,
+ *     so calls must not span a cudaDeviceReset (or any other teardown of
+ *     the device's primary context).
  *   - Allocates nothing: no cudaMalloc / cudaFree or allocating library call.
  *   - All calls share the array: calls that overlap on the GPU (other
  *     streams, other host threads on the same device) race.  Nothing in it

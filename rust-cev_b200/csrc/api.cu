@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -28,6 +29,26 @@ int set_error(int code, const char* fmt, ...) {
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
+int opt_in_smem(const void* fn, int bytes, const char* what) {
+  struct Done {
+    const void* fn;
+    int dev, bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Done> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Done& d : done)
+    if (d.fn == fn && d.dev == dev && d.bytes >= bytes) return CEVK_OK;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return set_error(CEVK_E_CUDA, "%s: cannot opt in to %d B of shared memory: %s", what, bytes, cudaGetErrorString(e));
+  done.push_back(Done{fn, dev, bytes});
   return CEVK_OK;
 }
 

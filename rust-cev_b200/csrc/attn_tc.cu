@@ -572,13 +572,7 @@ static int launch_tc(const void* q, const void* k, const void* v, void* const* o
   if ((rc = make_map(&tq, q, D, hq, n_tokens, q_rs, group, rows_t))) return rc;
   if ((rc = make_map(&tk, k, D, hkv, n_kv_rows, kv_rs, 1, BN))) return rc;
   if ((rc = make_map(&tv, v, D, hkv, n_kv_rows, kv_rs, 1, BN))) return rc;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<D, BN, KSK, KSV, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
-        cudaSuccess)
-      return set_error(CEVK_E_CUDA, "cannot opt in to %d B of shared memory", C::SMEM);
-    attr = true;
-  }
+  if ((rc = opt_in_smem((const void*)attn_tc_kernel<D, BN, KSK, KSV, NT>, C::SMEM, "attn_tc_kernel"))) return rc;
   AttnParams prm;
   if (n_o < 1 || n_o > kMaxOut) return set_error(CEVK_E_SHAPE, "attention: %d output buffers (1..%d)", n_o, kMaxOut);
   for (int d = 0; d < kMaxOut; ++d) prm.o[d] = d < n_o ? reinterpret_cast<__nv_bfloat16*>(o[d]) : nullptr;

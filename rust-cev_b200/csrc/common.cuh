@@ -306,4 +306,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 namespace cevk {
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
+// Raises `fn`'s dynamic shared-memory limit to `bytes` on the current device,
+// once per (kernel, device): the attribute is per device, so a process that
+// launches on several GPUs opts in on each.  Thread-safe.
+int opt_in_smem(const void* fn, int bytes, const char* what);
 }  // namespace cevk

@@ -392,7 +392,7 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
       rc = gdn_tc_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,
                       nk, nv, dk, dv, st);
     } else {
-      cudaFuncSetAttribute(gdn_chunk_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if ((rc = opt_in_smem((const void*)gdn_chunk_kernel<__nv_bfloat16>, (int)smem, "gdn_chunk_kernel"))) return rc;
       gdn_chunk_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(prm);
       rc = check_launch("gdn_chunk_kernel");
     }
@@ -400,9 +400,10 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
     launch_gated_norm<__nv_bfloat16>(prm.core, (const __nv_bfloat16*)z, z_row_stride, (const __nv_bfloat16*)norm_w,
                                      eps, (__nv_bfloat16*)y, rows, nv, dv, st);
   } else if (dtype == CEVK_F32) {
-    cudaFuncSetAttribute(gdn_chunk_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int rc = opt_in_smem((const void*)gdn_chunk_kernel<float>, (int)smem, "gdn_chunk_kernel");
+    if (rc) return rc;
     gdn_chunk_kernel<float><<<grid, 256, smem, st>>>(prm);
-    int rc = check_launch("gdn_chunk_kernel");
+    rc = check_launch("gdn_chunk_kernel");
     if (rc) return rc;
     launch_gated_norm<float>(prm.core, (const float*)z, z_row_stride, (const float*)norm_w, eps, (float*)y, rows, nv,
                              dv, st);

@@ -722,17 +722,12 @@ size_t scan_smem() {
 
 template <int DK, int DV>
 int launch(const Params& p, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gdn_prep_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)prep_smem<DK, DV>()) != cudaSuccess ||
-        cudaFuncSetAttribute(gdn_scan_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)scan_smem<DK, DV>()) != cudaSuccess)
-      return set_error(CEVK_E_CUDA, "gdn: cannot opt in to the shared memory of the tensor-core kernels");
-    attr = true;
-  }
+  int rc;
+  if ((rc = opt_in_smem((const void*)gdn_prep_kernel<DK, DV>, (int)prep_smem<DK, DV>(), "gdn_prep_kernel")) ||
+      (rc = opt_in_smem((const void*)gdn_scan_kernel<DK, DV>, (int)scan_smem<DK, DV>(), "gdn_scan_kernel")))
+    return rc;
   gdn_prep_kernel<DK, DV><<<dim3(p.n_chunks, p.nv, p.B), 128, prep_smem<DK, DV>(), st>>>(p);
-  int rc = check_launch("gdn_prep_kernel");
+  rc = check_launch("gdn_prep_kernel");
   if (rc) return rc;
   gdn_scan_kernel<DK, DV><<<dim3(DV / VS, p.nv, p.B), SCAN_THREADS, scan_smem<DK, DV>(), st>>>(p);
   return check_launch("gdn_scan_kernel");

@@ -61,6 +61,31 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype, tol, B, T):
         assert (s_out - s_ref).abs().max().item() < tol
 
 
+def test_noalloc_at_the_cfg4_head_shape_takes_the_core_only_path_twice():
+    """A 512-token chunk at the cfg4 GDN shape (nk 16, nv 32, dk = dv = 128,
+    bf16): the tensor-core scratch does not fit the static array, so the call
+    runs the kernel whose only scratch is the f32 core output (8 MiB here).
+    Checked against the workspace entry point given exactly that much
+    workspace (the same kernel), on two calls in a row."""
+    from cev_b200 import ops
+    from cev_b200._lib import BF16, lib
+    B, T, nk, nv, dk, dv = 1, 512, 16, 32, 128, 128
+    core_bytes = B * T * nv * dv * 4
+    assert ops.gdn_workspace_size(B, T, nv, dk, dv) > (16 << 20) >= core_bytes
+    args = _inputs(B, T, nk, nv, dk, dv, torch.bfloat16, 78)
+    conv_out, ab, z, a_log, dt_bias, norm_w, s0 = args
+    s_ref = torch.empty(B, nv, dk, dv, device="cuda")
+    ws = torch.empty(core_bytes, dtype=torch.uint8, device="cuda")
+    y_ref = ops.gdn_chunk_prefill(conv_out, ab, ab.stride(0), z, z.stride(0), a_log, dt_bias, norm_w, 1e-6, s0, s_ref,
+                                  B, T, nk, nv, dk, dv, ws)
+    for _ in range(2):
+        y, s_out = _noalloc(lib(), *args, B, T, nk, nv, dk, dv, BF16)
+        torch.cuda.synchronize()
+        assert (y.float() - y_ref.float()).abs().max().item() <= 1e-2 * y_ref.float().abs().max().item()
+        assert (s_out - s_ref).abs().max().item() < 1e-4
+    assert lib().cevk_device_status() == 0
+
+
 def test_noalloc_rejects_sizes_over_the_static_array():
     from cev_b200._lib import E_SHAPE, F32, lib
     l = lib()
