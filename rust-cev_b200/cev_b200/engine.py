@@ -90,7 +90,9 @@ class Engine:
     def _plan(self, req: Request) -> _Plan:
         m = self.model
         if len(req.prefix) == 0:
-            raise InputError("empty shared prefix")
+            # an internal error, not a request fault: engine.rs:344-346
+            # bails (anyhow) rather than returning InputError
+            raise RuntimeError("empty shared prefix")
         longest = max(len(req.prefix) + len(s) for s in req.suffixes)
         if longest >= m.max_len:
             raise InputError(f"prompt is {longest} tokens; the context limit is {m.max_len}")

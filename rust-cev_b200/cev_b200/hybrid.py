@@ -319,7 +319,11 @@ class HybridEngine:
         """hybrid.rs:697-739 with the Codes readout of 619-641."""
         d = self.decoder
         if len(req.prefix) == 0:
-            raise InputError("empty shared prefix")
+            # hybrid.rs:480-484: a Codes request whose questions share no
+            # leading token bails (an internal error, not InputError); the
+            # state-less row path of hybrid.rs:701 serves only bidirectional
+            # whole-prompt rows
+            raise RuntimeError("empty shared prefix")
         longest = max(len(req.prefix) + len(s) for s in req.suffixes)
         if longest >= d.max_len:
             raise InputError(f"prompt is {longest} tokens; the context limit is {d.max_len}")

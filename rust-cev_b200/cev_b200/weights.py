@@ -126,11 +126,57 @@ def save(dirname: str, cfg: dict, weights: dict) -> None:
 
 
 def load(dirname: str, dtype=None, device="cpu"):
-    """Read the pair written by :func:`save`; returns (cfg, weights)."""
+    """Read ``config.json`` and every ``*.safetensors`` shard of a checkpoint
+    directory (the files ``RepoFiles::weights`` lists, load.rs); returns
+    (cfg, weights).  With ``dtype`` every tensor but the f32 GDN gate
+    parameters is cast to it."""
+    import glob
+
     from safetensors.torch import load_file
     with open(os.path.join(dirname, "config.json")) as f:
         cfg = json.load(f)
-    w = load_file(os.path.join(dirname, "model.safetensors"), device=str(device))
+    shards = sorted(glob.glob(os.path.join(dirname, "*.safetensors")))
+    if not shards:
+        raise FileNotFoundError(f"no *.safetensors in {dirname}")
+    w = {}
+    for sh in shards:
+        w.update(load_file(sh, device=str(device)))
     if dtype is not None:
         w = {k: (v if k.endswith(("A_log", "dt_bias")) else v.to(dtype)) for k, v in w.items()}
     return cfg, w
+
+
+def pick_dtype(name: str, device) -> torch.dtype:
+    """``EngineOptions::dtype`` (engine.rs:108-115): "auto" is bf16 on a CUDA
+    device and f32 elsewhere; "f32", "bf16" name theirs."""
+    dev = torch.device(device)
+    if name == "auto":
+        return torch.bfloat16 if dev.type == "cuda" else torch.float32
+    if name in ("f32", "float32"):
+        return torch.float32
+    if name in ("bf16", "bfloat16"):
+        return torch.bfloat16
+    raise ValueError(f"unknown dtype `{name}`")
+
+
+def load_decoder(dirname: str, dtype="auto", device="cuda", **kw):
+    """``cev_model::load`` (load.rs:326-337) at the model level: detect the
+    family from ``config.json``'s ``model_type`` and build it on ``device``
+    from the directory's safetensors.  Returns (cfg, model): a
+    :class:`cev_b200.qwen3.Qwen3` for ``qwen3``, a
+    :class:`cev_b200.hybrid.Qwen35` for ``qwen3_5`` / ``qwen3_5_text``, a
+    :class:`cev_b200.hybrid.Lfm2` for ``lfm2``.  ``kw`` go to the model's
+    constructor (``arena_rows``, ``max_len``, ...)."""
+    dt = pick_dtype(dtype, device) if isinstance(dtype, str) else dtype
+    cfg, w = load(dirname)
+    mt = cfg.get("model_type")
+    if mt == "qwen3":
+        from .qwen3 import Qwen3
+        return cfg, Qwen3(cfg, w, dt, device, **kw)
+    if mt in ("qwen3_5", "qwen3_5_text"):
+        from .hybrid import Qwen35
+        return cfg, Qwen35(cfg, w, dt, device, **kw)
+    if mt == "lfm2":
+        from .hybrid import Lfm2
+        return cfg, Lfm2(cfg, w, dt, device, **kw)
+    raise ValueError(f"unsupported model_type `{mt}`")

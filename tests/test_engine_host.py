@@ -112,8 +112,24 @@ def test_plan_rejects_a_prompt_at_the_context_limit():
         eng._plan(Request([1] * 100, [[2] * 20, [3] * 28], [1, 1]))
     with pytest.raises(InputError, match="context limit"):
         eng._plan(Request([1] * 128, [[2]], [1]))
-    with pytest.raises(InputError, match="empty shared prefix"):
+    # engine.rs:344-346 bails: an internal error, not a request fault
+    with pytest.raises(RuntimeError, match="empty shared prefix") as e:
         eng._plan(Request([], [[2]], [1]))
+    assert not isinstance(e.value, InputError)
+
+
+def test_hybrid_engine_rejects_an_empty_prefix_as_an_internal_error():
+    """hybrid.rs:480-484: a Codes request whose questions share no leading
+    token bails before any forward (not InputError); a prompt at the context
+    limit is an InputError (hybrid.rs:485-488)."""
+    from cev_b200.hybrid import HybridEngine
+    eng = HybridEngine.__new__(HybridEngine)
+    eng.decoder = SimpleNamespace(max_len=64)
+    with pytest.raises(RuntimeError, match="empty shared prefix") as e:
+        eng.run(Request([], [[1, 2]], [1]))
+    assert not isinstance(e.value, InputError)
+    with pytest.raises(InputError, match="context limit is 64"):
+        eng.run(Request([1] * 60, [[2] * 4], [1]))
 
 
 def test_plan_reuses_and_pins_a_cached_prefix():
