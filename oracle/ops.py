@@ -75,10 +75,26 @@ def attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor
     d = q.shape[-1]
     scale = 1.0 / math.sqrt(d)
     g = q.shape[1] // k.shape[1]
-    kk, vv = repeat_kv(k, g), repeat_kv(v, g)
-    scores = torch.matmul(q, kk.transpose(-1, -2)).float() * scale + mask.float()
-    p = torch.softmax(scores, dim=-1).to(v.dtype)
-    return torch.matmul(p, vv)
+    b, hq, t, _ = q.shape
+    s = k.shape[2]
+    if b * hq * t * s <= (1 << 27):
+        kk, vv = repeat_kv(k, g), repeat_kv(v, g)
+        scores = torch.matmul(q, kk.transpose(-1, -2)).float() * scale + mask.float()
+        p = torch.softmax(scores, dim=-1).to(v.dtype)
+        return torch.matmul(p, vv)
+    # Large shapes (long states at the benchmark configs): the same
+    # arithmetic one query head at a time, so that the f32 score matrix
+    # held at once is (B, 1, T, S) instead of (B, Hq, T, S).  Every row's
+    # softmax is independent of the other heads, so the result is the same.
+    out = torch.empty(b, hq, t, v.shape[-1], dtype=v.dtype)
+    m = mask.float()
+    per_head = m.dim() == 4 and m.shape[1] == hq
+    for h in range(hq):
+        mh = m[:, h:h + 1] if per_head else m
+        sc = torch.matmul(q[:, h:h + 1], k[:, h // g:h // g + 1].transpose(-1, -2)).float() * scale + mh
+        p = torch.softmax(sc, dim=-1).to(v.dtype)
+        out[:, h:h + 1] = torch.matmul(p, v[:, h // g:h // g + 1])
+    return out
 
 
 def segment_mask(segments: list[int], past: int) -> torch.Tensor:

@@ -434,3 +434,43 @@ def test_bounded_wait_gives_up_reports_and_leaves_the_context_usable():
     out = ops.attend_packed(q, k, v, plan)
     ops.device_status()
     check_bf16_attention(out, q, k, v, segs, n_tok)
+
+
+def test_head_gather_wait_gives_up_when_a_peer_never_signals():
+    """The fused head all-gather's bounded wait on one GPU: (1) with both
+    ranks' flags raised (the two signals issued from this process, in
+    stream order before the wait) the wait passes; (2) with a peer whose
+    flag never reaches the epoch the wait gives up after ~2M cycles,
+    cevk_device_status reports CEVK_E_TIMEOUT naming the head all-gather
+    and the silent rank, the record clears, and the next attention call
+    still matches the oracle.  Nothing waits on another process, so no
+    kernel depends on a concurrent one."""
+    import ctypes as C
+
+    from cev_b200 import _lib, ops
+    lib = _lib.lib()
+    assert lib.cevk_device_status() == _lib.OK
+    ptr = C.c_void_p()
+    assert lib.cevk_ipc_alloc(256, C.byref(ptr)) == _lib.OK  # zeroed int32[64]
+    try:
+        flags = (C.c_void_p * 2)(ptr, ptr)  # both "ranks" publish into this one array
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for r in (0, 1):
+            assert lib.cevk_gather_signal(flags, 2, r, 1, st) == _lib.OK
+        assert lib.cevk_gather_wait(ptr, 2, 1, 1 << 21, st) == _lib.OK
+        assert lib.cevk_device_status() == _lib.OK
+        # epoch 2: rank 0 signals, rank 1 never does
+        assert lib.cevk_gather_signal(flags, 2, 0, 2, st) == _lib.OK
+        assert lib.cevk_gather_wait(ptr, 2, 2, 1 << 21, st) == _lib.OK
+        assert lib.cevk_device_status() == _lib.E_TIMEOUT
+        msg = lib.cevk_last_error().decode()
+        assert "head all-gather" in msg and "rank 1" in msg and "epoch 2" in msg, msg
+        assert lib.cevk_device_status() == _lib.OK
+    finally:
+        assert lib.cevk_ipc_free(ptr) == _lib.OK
+    hq, hkv, D, segs, n_tok, n_kv = CASES[2]
+    q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 501)
+    plan = ops.AttnPlan(segs, n_tok, n_kv, hq, hkv, D, torch.bfloat16, "cuda")
+    out = ops.attend_packed(q, k, v, plan)
+    ops.device_status()
+    check_bf16_attention(out, q, k, v, segs, n_tok)

@@ -121,3 +121,22 @@ def test_bidirectional_mask_restates_the_reference():
     inf = float("-inf")
     assert m[0].tolist() == [[0, 0, inf, inf], [0, 0, inf, inf], [0, 0, 0, inf], [0, 0, inf, 0]]
     assert m[1].tolist() == [[0, inf, inf, inf], [inf, 0, inf, inf], [inf, inf, 0, inf], [inf, inf, inf, 0]]
+
+
+def test_attend_head_by_head_equals_all_heads_at_once():
+    """The oracle's memory-bounded attention (one query head at a time, for
+    the long states of the benchmark configs) computes what the all-heads
+    form does (qwen3.rs:206-220), for a 2-D causal mask and a per-row 4-D
+    one."""
+    g = torch.Generator().manual_seed(3)
+    b, hq, hkv, t, past, d = 2, 4, 2, 300, 120000, 16
+    q = torch.randn(b, hq, t, d, generator=g)
+    k = torch.randn(b, hkv, past + t, d, generator=g)
+    v = torch.randn(b, hkv, past + t, d, generator=g)
+    assert b * hq * t * (past + t) > (1 << 27)  # takes the head-by-head path
+    for mask in (ops.causal_mask(t, past), ops.causal_mask(t, past)[None, None].expand(b, 1, t, past + t)):
+        got = ops.attend(q, k, v, mask)
+        kk, vv = ops.repeat_kv(k, 2), ops.repeat_kv(v, 2)
+        sc = torch.matmul(q, kk.transpose(-1, -2)) * d ** -0.5 + mask
+        want = torch.matmul(torch.softmax(sc, -1), vv)
+        assert (got - want).abs().max().item() < 1e-5
