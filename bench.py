@@ -129,7 +129,7 @@ def run_reference(args, rank, world):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
 
     k = rn(1, hkv, P + n_suf * L, D)
-    v = torch.randn(1, hkv, P + n_suf * L, D, generator=g)
+    v = rn(1, hkv, P + n_suf * L, D)
     q = rn(1, hq, n_suf * L, D)
     # one request packed the reference way: K/V concatenated, additive mask
     # over [prefix | all suffixes], each suffix sees the prefix and itself causally
@@ -151,7 +151,8 @@ def run_reference(args, rank, world):
             "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "sample": sample},
-            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "cpu": cpu_model(), "kind": "port",
+                             "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -176,30 +177,193 @@ def cpu_baseline_sample():
         ref.attend(q, x, x, mask)
         reps += 1
     dt = (time.perf_counter() - t0) / reps
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "cpu": cpu_model(), "kind": "port",
             "sample": f"1 request prefix + {n_suf} suffixes, f32 torch CPU, {reps} reps over ~10 s"}
 
 
-def decisions_bench(n_req: int, dev, world: int, dist_mod):
+def cpu_model() -> str:
+    """The host CPU's model name (for the CPU-baseline records)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+GDN_CHUNK = 64
+
+
+def _layer_linear_params(cfg: dict, kind: str) -> int:
+    """Weights one token multiplies through in one layer of ``kind`` (its
+    projections and its MLP), i.e. half the linear FLOPs per token."""
+    h, inter = cfg["hidden_size"], cfg["intermediate_size"]
+    hq, hkv = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    D = cfg.get("head_dim") or h // hq
+    mlp = 3 * h * inter
+    if kind == "attn":
+        qo = 2 * hq * D if cfg.get("attn_output_gate", False) else hq * D
+        return h * (qo + 2 * hkv * D) + hq * D * h + mlp
+    if kind == "gdn":
+        nk, nv = cfg["linear_num_key_heads"], cfg["linear_num_value_heads"]
+        dk, dv = cfg["linear_key_head_dim"], cfg["linear_value_head_dim"]
+        C = 2 * nk * dk + nv * dv
+        return h * (C + nv * dv + 2 * nv) + nv * dv * h + mlp
+    if kind == "conv":
+        return h * 3 * h + h * h + mlp
+    raise ValueError(kind)
+
+
+def request_flops(cfg: dict, prefix_len: int, row_lens, n_codes: int) -> float:
+    """Algorithmic FLOPs of one decision request: a ``prefix_len``-token
+    state, causal over itself, then ``row_lens`` question rows (suffixes or
+    right-padded rows: their real tokens only), each seeing the whole state
+    and itself causally.  Counts the projection / MLP GEMMs (2 FLOP per MAC
+    per real token), attention on visible (query, key) pairs only
+    (4 * head_dim * Hq per pair), the GDN chunked delta rule per token and
+    value head (2 C (3 dk + 2 dv) + 6 dk dv with C = 64) and the code
+    readout; padding, masked pairs and the conv taps are not counted."""
+    h = cfg["hidden_size"]
+    hq = cfg["num_attention_heads"]
+    D = cfg.get("head_dim") or h // hq
+    types = cfg.get("layer_types") or ["full_attention"] * cfg["num_hidden_layers"]
+    tokens = prefix_len + sum(row_lens)
+    pairs = prefix_len * (prefix_len + 1) // 2 + sum(n * prefix_len + n * (n + 1) // 2 for n in row_lens)
+    total = 0.0
+    for t in types:
+        kind = {"full_attention": "attn", "linear_attention": "gdn", "conv": "conv"}[t]
+        total += 2.0 * _layer_linear_params(cfg, kind) * tokens
+        if kind == "attn":
+            total += 4.0 * D * hq * pairs
+        elif kind == "gdn":
+            dk, dv = cfg["linear_key_head_dim"], cfg["linear_value_head_dim"]
+            total += (2.0 * GDN_CHUNK * (3 * dk + 2 * dv) + 6.0 * dk * dv) * cfg["linear_num_value_heads"] * tokens
+    return total + 2.0 * h * n_codes * len(row_lens)
+
+
+def decision_rows(name: str, qs, codes, max_permutations: int = 2):
+    """Row lengths a request's questions become (every rotation variant's
+    rendered suffix), as the engines run them."""
+    from cev_b200 import service, workloads
+    mode = "none" if name == "cfg5" else "permute"
+    out = []
+    for q in qs:
+        for s in service.shifts(mode, len(q.options), max_permutations):
+            out.append(len((q if s == 0 else q.rotated(s)).render(codes, workloads.SEP_ID)))
+    return out
+
+
+def cpu_decisions_baseline(name: str, dev) -> dict:
+    """The reference algorithm (the CPU oracle, bf16 like the config) on the
+    host cores for one request of config ``name``, timed on a bounded sample:
+    the whole request through models of 0 layers and of one layer of each
+    kind the config has, then t = t0 + sum over kinds of n_kind * (t_kind -
+    t0) for the config's full layer count.  Weights are seeded random-init
+    generated on the GPU and copied to the host."""
+    import torch
+    sys.path.insert(0, ROOT)
+    from cev_b200 import configs, weights, workloads
+    from oracle import engine as oeng
+    from oracle import hybrid as ohyb
+    from oracle import qwen3 as oq3
+    from oracle import service as osvc
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    full = configs.get(name)
+    codes = workloads.code_ids(4)
+    if name == "cfg3":
+        prefix, qs = workloads.decision_request(1, 8192, 32, 48, 128, 4, 151643)
+        kinds = {"attn": ["full_attention"]}
+        counts = {"attn": full["num_hidden_layers"]}
+    elif name == "cfg4":
+        prefix, qs = workloads.decision_request(2, 16384, 32, 32, 128, 4, full["vocab_size"] - 1)
+        kinds = {"gdn": ["linear_attention"], "attn": ["full_attention"]}
+        counts = {"gdn": full["layer_types"].count("linear_attention"),
+                  "attn": full["layer_types"].count("full_attention")}
+    else:
+        prefix, qs = workloads.decision_request(3, 65536, 64, 64, 64, 4, full["vocab_size"] - 1)
+        kinds = {"conv": ["conv"], "attn": ["full_attention"]}
+        counts = {"conv": full["layer_types"].count("conv"), "attn": full["layer_types"].count("full_attention")}
+    oq = [osvc.Question(q.head, q.options, q.tail, list(q.order)) for q in qs]
+    mode = "none" if name == "cfg5" else "permute"
+
+    def run(types):
+        cfg = configs.get(name)
+        cfg["num_hidden_layers"] = len(types)
+        if "layer_types" in cfg:
+            cfg["layer_types"] = list(types)
+        w = {k: v.cpu() for k, v in weights.init_weights(cfg, 7, torch.float32, dev).items()}
+        if name == "cfg3":
+            eng = oeng.Engine(oq3.Qwen3(cfg, w, torch.bfloat16), codes, prefill_chunk=512, pass_tokens=16384)
+        elif name == "cfg4":
+            eng = ohyb.HybridEngine(ohyb.Qwen35(cfg, w, torch.bfloat16), codes, pad_id=0, prefill_chunk=16384,
+                                    pass_tokens=8192, prefix_cache_tokens=16384)
+        else:
+            eng = ohyb.HybridEngine(ohyb.Lfm2(cfg, w, torch.bfloat16), codes, pad_id=0, prefill_chunk=512,
+                                    pass_tokens=8192, prefix_cache_tokens=65536)
+        del w
+        t0 = time.perf_counter()
+        osvc.run_debiased(eng, prefix, oq, mode, codes, workloads.SEP_ID, max_permutations=2)
+        return time.perf_counter() - t0
+
+    t_base = run([])
+    t_req = t_base
+    parts = {}
+    for k, types in kinds.items():
+        tk = run(types)
+        parts[k] = tk - t_base
+        t_req += counts[k] * max(tk - t_base, 0.0)
+    n_dec = len(qs)
+    return {"value": n_dec / t_req, "unit": "decisions/s", "cores": cores, "cpu": cpu_model(), "kind": "port",
+            "sample": f"one {name} request ({n_dec} questions) through the bf16 CPU oracle with 0 layers "
+                      f"({t_base:.1f} s) and one layer of each kind "
+                      + ", ".join(f"{k} +{v:.1f} s" for k, v in parts.items())
+                      + f", extrapolated to {sum(counts.values())} layers: {t_req:.1f} s per request"}
+
+
+def _sustained_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured bf16 sustained"
+    except Exception:
+        return 1400.0, "fallback bf16 sustained"
+
+
+def _roofline(flops_total: float, seconds: float, world: int) -> dict:
+    """Tensor roofline of a decisions run: algorithmic FLOPs / s per GPU
+    against the sustained cuBLAS bf16 figure (decision runs are long,
+    power-capped steps)."""
+    peak, src = _sustained_peak()
+    per_gpu = flops_total / seconds / world / 1e12
+    return {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
+            "peak_source": src, "flop_total": flops_total}
+
+
+def decisions_bench(n_req: int, dev, world: int, dist_mod, batch: int = 8):
     """cfg3: Qwen3-8B-shaped decoder (bf16, random init seed 1); per request
     an 8192-token random-id state (head 7680 prefilled in 512-token chunks,
     tail 512 in the packed pass) and 32 questions of U[48,128] tokens with 4
     option codes x 2 rotations, all 64 suffixes in one packed pass; served
     probabilities on the host.  Decisions = questions answered.  Timed end to
-    end: token ids in from the host, probabilities out, this rank's requests
-    served by one run_many call."""
+    end: token ids in from the host, probabilities out; this rank's
+    ``n_req`` requests (the config's 256 over 8 GPUs is 32 per GPU) served
+    ``batch`` per run_many call."""
     import torch
     from cev_b200 import configs, service, weights, workloads
     from cev_b200.engine import Engine
     from cev_b200.qwen3 import Qwen3
     cfg = configs.get("cfg3")
     w = weights.init_weights(cfg, 1, torch.bfloat16, dev)
-    model = Qwen3(cfg, w, torch.bfloat16, dev, arena_rows=65536 + 16384)
+    model = Qwen3(cfg, w, torch.bfloat16, dev, arena_rows=batch * 8192 + 16384)
     del w
     codes = workloads.code_ids(4)
-    eng = Engine(model, codes, prefill_chunk=512, pass_tokens=16384)
+    eng = Engine(model, codes, prefill_chunk=512, pass_tokens=16384, prefix_cache_tokens=batch * 8192)
     rank = int(os.environ.get("RANK", "0"))
     reqs = [workloads.decision_request(10_000 * (rank + 1) + i, 8192, 32, 48, 128, 4, 151643) for i in range(n_req + 1)]
+    flops = sum(request_flops(cfg, len(p), decision_rows("cfg3", qs, codes), len(codes)) for p, qs in reqs[1:])
 
     def one(prefix, qs):
         return service.run_debiased(eng, prefix, qs, "permute", codes, workloads.SEP_ID, max_permutations=2)
@@ -210,20 +374,24 @@ def decisions_bench(n_req: int, dev, world: int, dist_mod):
     if world > 1:
         dist_mod.barrier()
     t0 = time.perf_counter()
-    # all of this rank's requests in one run_many: their prefill chunks and
+    # each run_many call serves `batch` requests: their prefill chunks and
     # question passes share passes (each request's results are its own)
-    results = service.run_debiased_many(eng, reqs[1:], "permute", codes, workloads.SEP_ID, max_permutations=2)
-    assert len(results) == n_req and all(len(probs) == 32 for _, probs in results)
+    for b0 in range(1, n_req + 1, batch):
+        results = service.run_debiased_many(eng, reqs[b0:b0 + batch], "permute", codes, workloads.SEP_ID,
+                                            max_permutations=2)
+        assert all(len(probs) == 32 for _, probs in results)
     torch.cuda.synchronize()
     dt = torch.tensor([time.perf_counter() - t0], device=dev)
+    fl = torch.tensor([flops], device=dev, dtype=torch.float64)
     if world > 1:
         dist_mod.all_reduce(dt, op=dist_mod.ReduceOp.MAX)
+        dist_mod.all_reduce(fl)
     n_dec = 32 * n_req * world
-    flop = 7.47e12 * n_dec
+    del eng, model
     return {"value": n_dec / dt.item(), "unit": "decisions/s", "requests_per_gpu": n_req,
-            "batching": f"{n_req} requests per run_many call",
+            "requests_total": n_req * world, "batching": f"{batch} requests per run_many call",
             "seconds": dt.item(), "workload": "cfg3 Qwen3-8B-shaped bf16, 8192-token state, 32 questions x 2 rotations",
-            "approx_tflops": flop / dt.item() / 1e12}
+            "parallelism": f"dp{world}", "roofline": _roofline(fl.item(), dt.item(), world)}
 
 
 def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
@@ -235,7 +403,7 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     2 rotations per question (cfg4) / none (cfg5).  Decisions/s end to end.
     With N > 1 GPUs cfg4 runs its own requests on every rank; cfg5 runs one
     request stream on all ranks with the attention layers split by KV-head
-    group (one NCCL all-gather of head outputs per attention layer)."""
+    group (the head outputs gathered by the attention epilogue over NVLink)."""
     import torch
     from cev_b200 import configs, hybrid, service, weights, workloads
     cfg = configs.get(name)
@@ -263,6 +431,7 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     vocab = cfg["vocab_size"] - 1
     stream = 0 if split is not None else rank  # a split model runs the same requests on every rank
     reqs = [workloads.decision_request(20_000 * (stream + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]
+    flops = sum(request_flops(cfg, len(p), decision_rows(name, qs, codes), len(codes)) for p, qs in reqs[1:])
 
     def one(prefix, qs):
         return service.run_debiased(eng, prefix, qs, mode, codes, workloads.SEP_ID, max_permutations=2)
@@ -286,9 +455,11 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
         gather = "fused into the attention epilogue (NVLink peer stores)" if split.fused else "NCCL all-gather"
         if split.fused is not None:
             split.fused.close()
+    del eng, dec
     return {"value": nq * n_req * streams / dt.item(), "unit": "decisions/s", "requests_per_stream": n_req,
             "seconds": dt.item(), "workload": f"{name}: {plen}-token state, {nq} questions, rows continuing the state",
-            "parallelism": f"kv-head split x{world}" if split is not None else f"dp{world}", "head_gather": gather}
+            "parallelism": f"kv-head split x{world}" if split is not None else f"dp{world}", "head_gather": gather,
+            "roofline": _roofline(flops * streams, dt.item(), world)}
 
 
 def timed(fn, steps, warmup, stream):
@@ -411,10 +582,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cevk")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--decisions", type=int, default=4,
-                    help="also measure cfg3 decisions/sec on this many requests per GPU (0 = skip)")
-    ap.add_argument("--hybrid", type=int, default=0,
-                    help="also measure cfg4 and cfg5 decisions/sec on this many requests per GPU")
+    ap.add_argument("--decisions", type=int, default=32,
+                    help="also measure cfg3 decisions/sec on this many requests per GPU (0 = skip; the config's "
+                         "256 requests over 8 GPUs are 32 per GPU)")
+    ap.add_argument("--batch", type=int, default=8, help="cfg3 requests per run_many call")
+    ap.add_argument("--hybrid", type=int, default=4,
+                    help="also measure cfg4 and cfg5 decisions/sec on this many requests per GPU (0 = skip)")
     ap.add_argument("--op", default="attn", choices=["attn", "gdn", "conv", "chunk", "cfg3", "cfg4", "cfg5"],
                     help="attn: the headline line; gdn / conv / chunk: one kernel at its layer shape; "
                          "cfg3/4/5: only that config's decisions/sec")
@@ -446,7 +619,7 @@ def main():
         if rank == 0:
             op_bench(args, dev)
     elif args.op in ("cfg3", "cfg4", "cfg5"):
-        res = (decisions_bench(args.requests, dev, world, dist) if args.op == "cfg3" else
+        res = (decisions_bench(args.requests, dev, world, dist, args.batch) if args.op == "cfg3" else
                hybrid_decisions_bench(args.op, args.requests, dev, world, dist))
         if rank == 0:
             print(json.dumps({"metric": f"{args.op} decisions/sec", **res}), flush=True)
@@ -571,14 +744,19 @@ def main():
     if args.decisions > 0 or args.hybrid > 0:
         del wb, bufs, hq_, hk, hv, ho
         torch.cuda.empty_cache()
+    cpu_leg = rank == 0 and world == 1 and not args.no_cpu_baseline
     if args.decisions > 0:
-        line["decisions"] = decisions_bench(args.decisions, dev, world, dist)
+        line["decisions"] = decisions_bench(args.decisions, dev, world, dist, args.batch)
         torch.cuda.empty_cache()
+        if cpu_leg:
+            line["decisions"]["cpu_baseline"] = cpu_decisions_baseline("cfg3", dev)
     if args.hybrid > 0:
         for name in ("cfg4", "cfg5"):
             line[f"decisions_{name}"] = hybrid_decisions_bench(name, args.hybrid, dev, world, dist)
             torch.cuda.empty_cache()
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            if cpu_leg:
+                line[f"decisions_{name}"]["cpu_baseline"] = cpu_decisions_baseline(name, dev)
+    if cpu_leg:
         line["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:
         print(json.dumps(line), flush=True)

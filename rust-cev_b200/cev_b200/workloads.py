@@ -2,10 +2,10 @@
 
 ``attention_batch`` builds the packed-prefill attention microbenchmark
 (cfg2): ``n_req`` requests, each a cached prefix of ``prefix`` K/V rows plus
-``n_suf`` question suffixes of ``suf_len`` tokens.  Q/K/V are drawn N(0, 1);
-Q and K are RMS-normalised per head and rotated with RoPE at their positions
-(prefix rows at 0..P-1, every suffix restarting at P) by the library's own
-norm+RoPE kernel, which also writes K/V into the arena.  Arena layout per
+``n_suf`` question suffixes of ``suf_len`` tokens.  Q/K/V are drawn N(0, 1)
+and RMS-normalised per head; Q and K are normalised and rotated with RoPE at
+their positions (prefix rows at 0..P-1, every suffix restarting at P) by the
+library's own norm+RoPE kernel, which also writes K/V into the arena.  Arena layout per
 request: its prefix rows, then its suffixes' rows.
 """
 from __future__ import annotations
@@ -60,6 +60,10 @@ class AttentionBatch:
         ops.qk_norm_rope(raw, (0, D), hq * D, (hq + hkv) * D, hq, hkv, D, ones_d, ones_d, 1e-6, False, pos, theta, D,
                          self.q, self.k, self.v, rows)
         del raw
+        # V is RMS-normalised per head as well (Q and K were by the kernel)
+        vf = self.v.float()
+        self.v.copy_((vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dtype))
+        del vf
         self.segments = []
         for rq in range(n_req):
             for j in range(n_suf):
