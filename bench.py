@@ -258,70 +258,134 @@ def decision_rows(name: str, qs, codes, max_permutations: int = 2):
 
 def cpu_decisions_baseline(name: str, dev) -> dict:
     """The reference algorithm (the CPU oracle, bf16 like the config) on the
-    host cores for one request of config ``name``, timed on a bounded sample:
-    the whole request through models of 0 layers and of one layer of each
-    kind the config has, then t = t0 + sum over kinds of n_kind * (t_kind -
-    t0) for the config's full layer count.  Weights are seeded random-init
-    generated on the GPU and copied to the host."""
+    host cores for one request of config ``name``, timed on a bounded
+    sample: each kind of layer the config has runs alone (a one-layer
+    oracle model) over each work item of the request -- a prefill chunk at
+    a given past length, the packed question pass, the state pass, the
+    right-padded rows pass -- on synthetic activations and synthetic cached
+    states of the true lengths (the arithmetic does not depend on the
+    values).  Prefill-chunk times are fitted linearly in the past length and
+    summed over the request's chunks; the request's time is the sum over
+    its layers.  Decisions/s = questions per request / that time."""
     import torch
     sys.path.insert(0, ROOT)
     from cev_b200 import configs, weights, workloads
-    from oracle import engine as oeng
     from oracle import hybrid as ohyb
+    from oracle import ops as oops
     from oracle import qwen3 as oq3
-    from oracle import service as osvc
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
+    bf = torch.bfloat16
+    g = torch.Generator().manual_seed(5)
     full = configs.get(name)
     codes = workloads.code_ids(4)
-    if name == "cfg3":
-        prefix, qs = workloads.decision_request(1, 8192, 32, 48, 128, 4, 151643)
-        kinds = {"attn": ["full_attention"]}
-        counts = {"attn": full["num_hidden_layers"]}
-    elif name == "cfg4":
-        prefix, qs = workloads.decision_request(2, 16384, 32, 32, 128, 4, full["vocab_size"] - 1)
-        kinds = {"gdn": ["linear_attention"], "attn": ["full_attention"]}
-        counts = {"gdn": full["layer_types"].count("linear_attention"),
-                  "attn": full["layer_types"].count("full_attention")}
-    else:
-        prefix, qs = workloads.decision_request(3, 65536, 64, 64, 64, 4, full["vocab_size"] - 1)
-        kinds = {"conv": ["conv"], "attn": ["full_attention"]}
-        counts = {"conv": full["layer_types"].count("conv"), "attn": full["layer_types"].count("full_attention")}
-    oq = [osvc.Question(q.head, q.options, q.tail, list(q.order)) for q in qs]
-    mode = "none" if name == "cfg5" else "permute"
 
-    def run(types):
+    def one_layer(kind):
         cfg = configs.get(name)
-        cfg["num_hidden_layers"] = len(types)
+        cfg["num_hidden_layers"] = 1
+        cfg["vocab_size"] = 1024  # the embedding table is not timed
         if "layer_types" in cfg:
-            cfg["layer_types"] = list(types)
+            cfg["layer_types"] = [kind]
         w = {k: v.cpu() for k, v in weights.init_weights(cfg, 7, torch.float32, dev).items()}
-        if name == "cfg3":
-            eng = oeng.Engine(oq3.Qwen3(cfg, w, torch.bfloat16), codes, prefill_chunk=512, pass_tokens=16384)
-        elif name == "cfg4":
-            eng = ohyb.HybridEngine(ohyb.Qwen35(cfg, w, torch.bfloat16), codes, pad_id=0, prefill_chunk=16384,
-                                    pass_tokens=8192, prefix_cache_tokens=16384)
-        else:
-            eng = ohyb.HybridEngine(ohyb.Lfm2(cfg, w, torch.bfloat16), codes, pad_id=0, prefill_chunk=512,
-                                    pass_tokens=8192, prefix_cache_tokens=65536)
-        del w
+        return cfg, w
+
+    def timed_cpu(fn):
         t0 = time.perf_counter()
-        osvc.run_debiased(eng, prefix, oq, mode, codes, workloads.SEP_ID, max_permutations=2)
+        fn()
         return time.perf_counter() - t0
 
-    t_base = run([])
-    t_req = t_base
+    def rnd(*shape, dtype=bf):
+        return torch.randn(*shape, generator=g).to(dtype)
+
+    def chunks_total(t_at, n_chunks, chunk, pts):
+        """Sum of t(past) over chunks at past 0, chunk, ..., fitted
+        linearly through the measured points."""
+        xs = [p for p in pts]
+        ys = [t_at(p) for p in pts]
+        n = len(xs)
+        mx, my = sum(xs) / n, sum(ys) / n
+        var = sum((x - mx) ** 2 for x in xs)
+        b = sum((x - mx) * (y - my) for x, y in zip(xs, ys)) / var if var else 0.0
+        a = my - b * mx
+        return sum(a + b * (c * chunk) for c in range(n_chunks))
+
     parts = {}
-    for k, types in kinds.items():
-        tk = run(types)
-        parts[k] = tk - t_base
-        t_req += counts[k] * max(tk - t_base, 0.0)
+    if name == "cfg3":
+        prefix, qs = workloads.decision_request(1, 8192, 32, 48, 128, 4, 151643)
+        rows = decision_rows("cfg3", qs, codes)
+        cfg, w = one_layer("full_attention")
+        m = oq3.Qwen3(cfg, w, bf)
+        hkv, D = cfg["num_key_value_heads"], cfg["head_dim"]
+
+        def chunk(past):
+            kv = None if past == 0 else [oq3.LayerKv(rnd(1, hkv, past, D), rnd(1, hkv, past, D))]
+            ids = torch.randint(0, 1024, (512,), generator=g).tolist()
+            return timed_cpu(lambda: m.forward_packed(kv, ids, list(range(past, past + 512)),
+                                                      oops.segment_mask([0] * 512, past), [511], [(0, 512)]))
+
+        m.forward_packed(None, [1] * 16, list(range(16)), oops.segment_mask([0] * 16, 0), [15], [])  # warm-up
+        head = 8192 - 512
+        parts["prefill chunks"] = chunks_total(chunk, head // 512, 512, [0, head - 512])
+        seg = [0] * 512 + sum([[j + 1] * n for j, n in enumerate(rows)], [])
+        past = head
+        kv = [oq3.LayerKv(rnd(1, hkv, past, D), rnd(1, hkv, past, D))]
+        ids = torch.randint(0, 1024, (len(seg),), generator=g).tolist()
+        parts["packed pass"] = timed_cpu(lambda: m.forward_packed(kv, ids, list(range(len(seg))),
+                                                                  oops.segment_mask(seg, past), [len(seg) - 1], [(0, 512)]))
+        t_req = full["num_hidden_layers"] * sum(parts.values())
+        n_layers = {"attention": full["num_hidden_layers"]}
+    else:
+        hybrid_cfg4 = name == "cfg4"
+        plen = 16384 if hybrid_cfg4 else 65536
+        prefix, qs = workloads.decision_request(2 if hybrid_cfg4 else 3, plen, 32 if hybrid_cfg4 else 64,
+                                                32 if hybrid_cfg4 else 64, 128 if hybrid_cfg4 else 64, 4,
+                                                full["vocab_size"] - 1)
+        rows = decision_rows(name, qs, codes)
+        H = full["hidden_size"]
+        kinds = ["linear_attention", "full_attention"] if hybrid_cfg4 else ["conv", "full_attention"]
+        t_req = 0.0
+        n_layers = {}
+        for kind in kinds:
+            cfg, w = one_layer(kind)
+            dec = (ohyb.Qwen35 if hybrid_cfg4 else ohyb.Lfm2)(cfg, w, bf)
+            hkv = cfg["num_key_value_heads"]
+            D = cfg.get("head_dim") or H // cfg["num_attention_heads"]
+
+            def state(past):
+                if kind == "full_attention":
+                    st = ohyb.AttnState(rnd(1, hkv, past, D), rnd(1, hkv, past, D))
+                elif kind == "conv":
+                    st = ohyb.ConvState(rnd(1, H, cfg["conv_L_cache"] - 1))
+                else:
+                    C = 2 * dec.nk * dec.dk + dec.nv * dec.dv
+                    st = ohyb.GdnState(rnd(1, C, dec.kernel - 1), rnd(1, dec.nv, dec.dk, dec.dv, dtype=torch.float32))
+                return ohyb.PrefixState([st], past, past)
+
+            def run(b, t, past, keep):
+                st = state(past) if past > 0 else None
+                x = rnd(b, t, H)
+                return timed_cpu(lambda: dec.forward(x, list(range(past, past + t)), st, keep=keep))
+
+            run(1, 16, 0, True)  # warm-up
+            n = full["layer_types"].count(kind)
+            n_layers[kind] = n
+            if hybrid_cfg4:
+                t_state = run(1, plen, 0, True)  # the state runs once as one pass
+            else:
+                t_state = chunks_total(lambda p: run(1, 512, p, True), plen // 512, 512,
+                                       [0, plen // 2, plen - 512] if kind == "full_attention" else [512])
+            t_rows = run(len(rows), max(rows), plen, False)
+            parts[f"{kind} state"] = t_state
+            parts[f"{kind} rows"] = t_rows
+            t_req += n * (t_state + t_rows)
     n_dec = len(qs)
     return {"value": n_dec / t_req, "unit": "decisions/s", "cores": cores, "cpu": cpu_model(), "kind": "port",
-            "sample": f"one {name} request ({n_dec} questions) through the bf16 CPU oracle with 0 layers "
-                      f"({t_base:.1f} s) and one layer of each kind "
-                      + ", ".join(f"{k} +{v:.1f} s" for k, v in parts.items())
-                      + f", extrapolated to {sum(counts.values())} layers: {t_req:.1f} s per request"}
+            "sample": f"one {name} request ({n_dec} questions): each layer kind alone through the bf16 CPU oracle "
+                      "on synthetic states of the true lengths, per work item ("
+                      + ", ".join(f"{k} {v:.2f} s" for k, v in parts.items())
+                      + "; prefill chunks fitted linearly in the past length), summed over "
+                      + ", ".join(f"{v} {k}" for k, v in n_layers.items())
+                      + f" layers: {t_req:.1f} s per request"}
 
 
 def _sustained_peak():
@@ -433,7 +497,18 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     reqs = [workloads.decision_request(20_000 * (stream + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]
     flops = sum(request_flops(cfg, len(p), decision_rows(name, qs, codes), len(codes)) for p, qs in reqs[1:])
 
+    gate = None
+    if split is not None:
+        # every rank runs each request of the split model: check on the host
+        # that all peers are still there before a request's first launch
+        from cev_b200.health import StepGate
+        gate = StepGate(rank, world, deadline_s=120.0, prefix=f"cev/{name}")
+    step = [0]
+
     def one(prefix, qs):
+        if gate is not None:
+            step[0] += 1
+            gate.enter(step[0])
         return service.run_debiased(eng, prefix, qs, mode, codes, workloads.SEP_ID, max_permutations=2)
 
     one(*reqs[0])
@@ -519,13 +594,30 @@ def op_bench(args, dev):
         ms = timed(fn, args.steps, args.warmup, stream)
         ops.device_status()
         tf = flops / (ms / 1e3) / 1e12
+        # the cfg4 state pass: the 16384-token state run once through a GDN layer
+        Ts = 16384
+        conv_s = (torch.randn(Ts, C_, device=dev, generator=g) * 0.5).bfloat16()
+        ab_s = torch.randn(Ts, 2 * nv, device=dev, generator=g).bfloat16()
+        z_s = torch.randn(Ts, nv * dv, device=dev, generator=g).bfloat16()
+        ws_s = torch.empty(ops.gdn_workspace_size(1, Ts, nv, dk, dv), dtype=torch.uint8, device=dev)
+        y_s = torch.empty(Ts, nv * dv, dtype=torch.bfloat16, device=dev)
+
+        def fn_state():
+            ops.gdn_chunk_prefill(conv_s, ab_s, 2 * nv, z_s, nv * dv, a_log, dt_bias, norm_w, 1e-6, None, s_out, 1, Ts,
+                                  nk, nv, dk, dv, ws_s, out=y_s)
+        ms_s = timed(fn_state, max(3, args.steps // 10), 3, stream)
+        ops.device_status()
+        tf_s = gdn_flops(Ts, nv, dk, dv) / (ms_s / 1e3) / 1e12
         line = {"metric": "gdn chunked prefill TFLOP/s (cfg4 layer, one 512-token chunk)", "value": tf,
-                "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
+                "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
                 "config": {"workload": f"B{B} T{T} nk{nk} nv{nv} dk{dk} dv{dv}, chunk 64, state in/out",
                            "flop_per_step": flops, "bytes_per_step": nbytes},
-                "roofline": {"bound": "mma.sync issue rate (bf16 three-term split)", "achieved": tf,
-                             "unit": "TFLOP/s",
-                             "hbm_gbs": nbytes / (ms / 1e3) / 1e9, "hbm_peak_gbs": peak_hbm, "peak_source": src}}
+                "state_pass": {"workload": f"B1 T{Ts} (the cfg4 state run once through one GDN layer)",
+                               "tflops": tf_s, "ms": ms_s},
+                "roofline": {"bound": "tensor (tcgen05, bf16 three-term split; latency of the chunk-sequential scan)",
+                             "achieved": tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": tf / peak_tf,
+                             "peak_source": src + " bf16 burst",
+                             "hbm_gbs": nbytes / (ms / 1e3) / 1e9, "hbm_peak_gbs": peak_hbm}}
     elif args.op == "conv":
         # cfg5 gated short conv layer (d 2048, K 3) over a 16384-token run
         B, T, d, K = 1, 16384, 2048, 3
@@ -608,8 +700,9 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        # short process-group timeout, non-blocking NCCL communicator init
+        from cev_b200 import health
+        health.init_distributed("nccl", rank, world, timeout_s=120.0, device=dev)
 
     def barrier():
         if world > 1:

@@ -323,6 +323,10 @@ static size_t gdn_smem(int dk) {
 
 size_t gdn_tc_extra_floats(int B, int T, int nv, int dk, int dv);
 bool gdn_tc_supported(int dk, int dv);
+size_t gdn_umma_extra_floats(int B, int T, int nv);
+int gdn_umma_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
+                 const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv,
+                 cudaStream_t st);
 int gdn_tc_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
                const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv, int dk,
                int dv, cudaStream_t st);
@@ -334,9 +338,13 @@ using namespace cevk;
 extern "C" {
 
 size_t cevk_gdn_workspace_size(int32_t B, int32_t T, int32_t nv, int32_t dk, int32_t dv) {
-  // core output [B, T, nv, dv] f32, then (bf16 tensor-core path) the
-  // per-chunk W, q', k', U, intra and e^last of gdn_tc.cu.
-  return ((size_t)B * T * nv * dv + gdn_tc_extra_floats(B, T, nv, dk, dv)) * sizeof(float);
+  // core output [B, T, nv, dv] f32, then (bf16 tensor-core paths) the
+  // per-chunk operands of the scan: the tcgen05 kernels' records
+  // (gdn_umma.cu, dk = dv = 128, plus 16 bytes of alignment slack) or the
+  // W, q', k', U, intra and e^last of gdn_tc.cu (dk = dv = 64).
+  const size_t extra = dk == 128 && dv == 128 ? gdn_umma_extra_floats(B, T, nv) + 4
+                                              : gdn_tc_extra_floats(B, T, nv, dk, dv);
+  return ((size_t)B * T * nv * dv + extra) * sizeof(float);
 }
 
 int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride, const void* z,
@@ -387,8 +395,14 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
   const unsigned ng = (unsigned)((rows * nv + 7) / 8);
   if (dtype == CEVK_BF16) {
     int rc;
-    if (full_ws && gdn_tc_supported(dk, dv) && ((uintptr_t)conv_out & 15) == 0 && C % 8 == 0) {
-      // tensor cores (gdn_tc.cu): chunk-parallel prep + state scan
+    const bool aligned = ((uintptr_t)conv_out & 15) == 0 && C % 8 == 0 && ((uintptr_t)workspace & 15) == 0;
+    if (full_ws && aligned && dk == 128 && dv == 128) {
+      // tcgen05 UMMA with TMEM accumulators (gdn_umma.cu): chunk-parallel
+      // prep + state scan
+      rc = gdn_umma_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,
+                        nk, nv, st);
+    } else if (full_ws && aligned && gdn_tc_supported(dk, dv)) {
+      // mma.sync (gdn_tc.cu), dk = dv = 64
       rc = gdn_tc_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,
                       nk, nv, dk, dv, st);
     } else {
