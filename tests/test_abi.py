@@ -102,3 +102,52 @@ def test_split_plan_fills_one_wave_of_underfilled_calls():
     assert _plan(rows, 4096, 6144, 16, 8, 128)[1] == 1                       # 512 CTAs: already full
     assert _plan([(0, 128, 0, 65536, 65536)], 128, 65664, 16, 4, 256)[1] == 9   # 16 CTAs, one per SM at head_dim 256
     assert lib.cevk_attn_split_workspace_size(16, 8, 64, 1) == 0
+
+
+def test_static_library_links_into_a_plain_c_program(tmp_path):
+    """``libcevk.a`` (the objects plus their device-link object) links with
+    the host toolchain alone -- as cargo links it through a build.rs -- and
+    defines every entry point the header declares."""
+    import shutil
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "rust-cev_b200"))
+    import build as cevk_build
+    lib_a = cevk_build.build(static=True)
+    nm = subprocess.run(["nm", "-g", "--defined-only", lib_a], capture_output=True, text=True, check=True).stdout
+    defined = set(re.findall(r"\bT (cevk_[a-z0-9_]+)\b", nm))
+    assert set(declared()) <= defined, sorted(set(declared()) - defined)
+    if shutil.which("gcc") is None:
+        pytest.skip("no gcc")
+    src = tmp_path / "main.c"
+    src.write_text('#include <stdio.h>\n#include "cevk.h"\n'
+                   'int main(void) { printf("%d %zu\\n", cevk_version(), '
+                   'cevk_gdn_workspace_size(1, 64, 4, 64, 64)); return 0; }\n')
+    exe = tmp_path / "main"
+    cuda = "/usr/local/cuda/lib64"
+    subprocess.run(["gcc", "-I", os.path.join(root, "include"), str(src), lib_a, "-L" + cuda, "-lcudart", "-lcuda",
+                    "-lstdc++", "-lm", "-o", str(exe)], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True,
+                         env=dict(os.environ, LD_LIBRARY_PATH=cuda)).stdout.split()
+    assert out[0] == "100" and int(out[1]) == _lib.lib().cevk_gdn_workspace_size(1, 64, 4, 64, 64)
+
+
+def test_rust_bindings_match_the_header():
+    """The committed Rust binding crate (rust-cev_b200/rust/cevk-sys) binds
+    every entry point of the header with the same arity and the same
+    status / dtype constants (there is no Rust toolchain here to compile
+    it, so the check is textual)."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    rs = open(os.path.join(root, "rust-cev_b200", "rust", "cevk-sys", "src", "lib.rs")).read()
+    fns = {n: a for n, a in re.findall(r"pub fn (cevk_[a-z0-9_]+)\s*\(([^)]*)\)", rs, flags=re.S)}
+    assert set(fns) == set(declared()), sorted(set(fns) ^ set(declared()))
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    for name, args in fns.items():
+        m = re.search(name + r"\s*\(([^)]*)\)", text)
+        c_params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        rs_params = [p for p in args.split(",") if p.strip()]
+        assert len(rs_params) == len(c_params), f"{name}: rust {len(rs_params)} params, header {len(c_params)}"
+    for const, val in re.findall(r"#define (CEVK_[A-Z0-9_]+) \(?(-?\d+)\)?", open(HEADER).read()):
+        m = re.search(r"pub const " + const + r": \w+ = (-?\d+)", rs)
+        assert m and int(m.group(1)) == int(val), const
