@@ -662,6 +662,46 @@ def op_bench(args, dev):
         line["value"] = line["hq32_hkv8"]["split"]["tflops"]
         line["roofline"] = {"bound": "tensor", "achieved": line["value"], "peak": peak_tf, "unit": "TFLOP/s",
                             "frac": line["value"] / peak_tf, "peak_source": src}
+    elif args.op == "glue":
+        # the bandwidth-bound glue at the decision configs' shapes, inputs
+        # larger than L2: QK-norm + RoPE writing K/V into arena rows (cfg5
+        # and cfg3 attention layers, 16384 tokens), residual add + RMSNorm
+        # and SwiGLU (cfg3 hidden 4096 / intermediate 12288, 16384 tokens)
+        res = {}
+        n = 16384
+        for name, hq, hkv, D, theta in (("qk_norm_rope cfg5 (32/8/8 heads, D 64)", 32, 8, 64, 1e6),
+                                        ("qk_norm_rope cfg3 (32/8/8 heads, D 128)", 32, 8, 128, 1e6)):
+            qkv = torch.randn(n, (hq + 2 * hkv) * D, device=dev, generator=g).bfloat16()
+            q = torch.empty(n, hq, D, dtype=torch.bfloat16, device=dev)
+            ka = torch.empty(n, hkv, D, dtype=torch.bfloat16, device=dev)
+            va = torch.empty_like(ka)
+            wq = torch.ones(D, dtype=torch.bfloat16, device=dev)
+            pos = torch.arange(n, device=dev, dtype=torch.int32)
+            rows = torch.randperm(n, device=dev, generator=g).to(torch.int32)  # scattered arena rows
+            ms = timed(lambda: ops.qk_norm_rope(qkv, (0, D), hq * D, (hq + hkv) * D, hq, hkv, D, wq, wq, 1e-6, False,
+                                                pos, theta, D, q, ka, va, rows), args.steps, args.warmup, stream)
+            nbytes = 2 * qkv.numel() * 2 + n * 8  # read every head row once, write it once; ids
+            res[name] = {"us": ms * 1e3, "gbs": nbytes / (ms / 1e3) / 1e9}
+        H, I = 4096, 12288
+        x = torch.randn(n, H, device=dev, generator=g).bfloat16()
+        a = torch.randn(n, H, device=dev, generator=g).bfloat16()
+        wn = torch.ones(H, dtype=torch.bfloat16, device=dev)
+        o = torch.empty_like(x)
+        ms = timed(lambda: ops.add_rms_norm(x, a, wn, 1e-6, out=o), args.steps, args.warmup, stream)
+        res["add_rms_norm cfg3 (hidden 4096)"] = {"us": ms * 1e3, "gbs": 4 * x.numel() * 2 / (ms / 1e3) / 1e9}
+        gu = torch.randn(n, 2 * I, device=dev, generator=g).bfloat16()
+        so = torch.empty(n, I, dtype=torch.bfloat16, device=dev)
+        ms = timed(lambda: ops.swiglu(gu, out=so), args.steps, args.warmup, stream)
+        res["swiglu cfg3 (intermediate 12288)"] = {"us": ms * 1e3, "gbs": 3 * n * I * 2 / (ms / 1e3) / 1e9}
+        ops.device_status()
+        first = next(iter(res.values()))["gbs"]
+        line = {"metric": "bandwidth-bound glue GB/s (16384 tokens, bf16)", "value": first, "unit": "GB/s",
+                "steps": args.steps, "warmup": args.warmup, "dtype": "bf16", "kernels": res,
+                "config": {"workload": "QK-norm + RoPE (cfg5, cfg3 attention layers), residual add + RMSNorm, "
+                                       "SwiGLU at 16384 tokens; inputs larger than L2"},
+                "roofline": {"bound": "hbm", "achieved": first, "peak": peak_hbm, "unit": "GB/s",
+                             "frac": first / peak_hbm, "peak_source": src + " copy",
+                             "per_kernel_frac": {k: v["gbs"] / peak_hbm for k, v in res.items()}}}
     else:
         raise SystemExit(f"unknown --op {args.op}")
     print(json.dumps(line), flush=True)
@@ -680,8 +720,8 @@ def main():
     ap.add_argument("--batch", type=int, default=8, help="cfg3 requests per run_many call")
     ap.add_argument("--hybrid", type=int, default=4,
                     help="also measure cfg4 and cfg5 decisions/sec on this many requests per GPU (0 = skip)")
-    ap.add_argument("--op", default="attn", choices=["attn", "gdn", "conv", "chunk", "cfg3", "cfg4", "cfg5"],
-                    help="attn: the headline line; gdn / conv / chunk: one kernel at its layer shape; "
+    ap.add_argument("--op", default="attn", choices=["attn", "gdn", "conv", "chunk", "glue", "cfg3", "cfg4", "cfg5"],
+                    help="attn: the headline line; gdn / conv / chunk / glue: kernels at their layer shapes; "
                          "cfg3/4/5: only that config's decisions/sec")
     ap.add_argument("--requests", type=int, default=2, help="requests per GPU for --op cfg3/cfg4/cfg5")
     args = ap.parse_args()
@@ -708,7 +748,7 @@ def main():
         if world > 1:
             dist.barrier()
 
-    if args.op in ("gdn", "conv", "chunk"):
+    if args.op in ("gdn", "conv", "chunk", "glue"):
         if rank == 0:
             op_bench(args, dev)
     elif args.op in ("cfg3", "cfg4", "cfg5"):

@@ -4,8 +4,10 @@
 // Rotary::apply, the head transposes and the K/V concatenation
 // (qwen3.rs:190-200, qwen35.rs:529-541, lfm2.rs:147-156).
 //
-// One block per token (cos/sin computed once per token), one warp per head
-// row.  For head_dim 64 / 128 / 256 (qk_norm_rope_vec_kernel) a lane holds
+// bf16 with aligned rows (qk_norm_rope_rows_kernel): one warp per token, a
+// head row over D/8 lanes with 16-byte accesses.  Otherwise one block per
+// token (cos/sin computed once per token), one warp per head row.  For
+// head_dim 64 / 128 / 256 (qk_norm_rope_vec_kernel) a lane holds
 // D/32 consecutive elements and takes the rotation partner (d +- rot/2) from
 // another lane by shuffle; other shapes go through a shared-memory row so
 // the partner can live in any lane.  HBM-bound: each element is read once
@@ -215,6 +217,96 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
   }
 }
 
+// bf16, head_dim 64 / 128 / 256 with every row start 16-byte aligned: one
+// warp per token, a head row spread over D/8 lanes of eight consecutive
+// elements (one 16-byte load / store), 32/(D/8) head rows per warp step.
+// Each lane computes the cos / sin of its eight element slots once and
+// reuses them for all of the token's heads; the RMS is reduced over the
+// row's lanes and the rotation partner (d +- rot/2, in lane +- rot/16 with
+// the same slot) comes by shuffle.
+template <int D>
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_rows_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int row_stride, int q_head_stride, int k_col, int v_col,
+    const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps, int plus_one,
+    const int32_t* __restrict__ pos, const InvFreq inv, int rot, __nv_bfloat16* __restrict__ q_out,
+    __nv_bfloat16* __restrict__ k_arena, __nv_bfloat16* __restrict__ v_arena, int kv_rs,
+    const int32_t* __restrict__ kv_rows, int hq, int hkv, int n_tokens) {
+  constexpr int L = D / 8;   // lanes per head row
+  constexpr int R = 32 / L;  // head rows per warp step
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= n_tokens) return;  // warp-uniform
+  const int sub = lane / L, d0 = (lane % L) * 8, half = rot / 2;
+  const float p = (float)pos[t];
+  float c[8], s[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int d = d0 + e;
+    c[e] = 1.f;
+    s[e] = 0.f;
+    if (d < rot) {
+      float sn, cs;
+      sincosf(p * inv.v[d < half ? d : d - half], &sn, &cs);
+      c[e] = cs;
+      s[e] = d < half ? -sn : sn;
+    }
+  }
+  const int partner = d0 < half ? lane + half / 8 : (d0 < rot ? lane - half / 8 : lane);
+  const float add = plus_one ? 1.f : 0.f;
+  const size_t kv_row = (size_t)kv_rows[t];
+  const __nv_bfloat16* row = qkv + (size_t)t * row_stride;
+  const int heads = hq + 2 * hkv;
+  // U steps' loads go out back to back before any of them is used, so a
+  // warp keeps U 16-byte loads in flight
+  constexpr int U = 6;
+  auto src_of = [&](int h) -> const __nv_bfloat16* {
+    return h < hq ? row + (size_t)h * q_head_stride
+                  : (h < hq + hkv ? row + k_col + (size_t)(h - hq) * D : row + v_col + (size_t)(h - hq - hkv) * D);
+  };
+  auto dst_of = [&](int h) -> __nv_bfloat16* {
+    return h < hq ? q_out + ((size_t)t * hq + h) * D
+                  : (h < hq + hkv ? k_arena + kv_row * kv_rs + (size_t)(h - hq) * D
+                                  : v_arena + kv_row * kv_rs + (size_t)(h - hq - hkv) * D);
+  };
+  for (int h0 = 0; h0 < heads; h0 += R * U) {
+    uint4 raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int h = h0 + u * R + sub;
+      raw[u] = h < heads ? *reinterpret_cast<const uint4*>(src_of(h) + d0) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int h = h0 + u * R + sub;
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+      float x[8], ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        x[i] = __bfloat162float(e[i]);
+        ss += x[i] * x[i];
+      }
+#pragma unroll
+      for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float r = rsqrtf(ss / D + eps);
+      float wv[8];  // the norm weight (L1-resident, shared by every token)
+      load_row<__nv_bfloat16, 8>((h < hq ? qw : kw) + d0, wv);
+      float y[8];
+      // Like the reference, the normed value is in the model dtype before RoPE.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = to_f(from_f<__nv_bfloat16>(x[i] * r * (wv[i] + add)));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = y[i] * c[i] + __shfl_sync(0xffffffffu, y[i], partner) * s[i];
+      if (h < heads) {
+        if (h < hq + hkv) {
+          store_row<__nv_bfloat16, 8>(dst_of(h) + d0, y);
+        } else {
+          *reinterpret_cast<uint4*>(dst_of(h) + d0) = raw[u];  // V: a plain copy
+        }
+      }
+    }
+  }
+}
+
 }  // namespace cevk
 
 using namespace cevk;
@@ -246,6 +338,25 @@ extern "C" int cevk_qk_norm_rope(const void* qkv, int32_t row_stride, int32_t q_
                    kv_row_stride % E == 0 &&
                    (((uintptr_t)qkv | (uintptr_t)q_out | (uintptr_t)k_arena | (uintptr_t)v_arena |
                      (uintptr_t)q_norm_w | (uintptr_t)k_norm_w) % (E * es)) == 0;
+  // bf16 rows on 16-byte boundaries, rotation halves in whole 8-element slots
+  const bool rows8 = dtype == CEVK_BF16 && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+                     (rotary_dim / 2) % 8 == 0 && row_stride % 8 == 0 && q_head_stride % 8 == 0 && k_col % 8 == 0 &&
+                     v_col % 8 == 0 && kv_row_stride % 8 == 0 &&
+                     (((uintptr_t)qkv | (uintptr_t)q_out | (uintptr_t)k_arena | (uintptr_t)v_arena |
+                       (uintptr_t)q_norm_w | (uintptr_t)k_norm_w) % 16) == 0;
+  if (rows8) {
+    const unsigned grid = (unsigned)((n_tokens + 7) / 8);
+#define CEVK_ROPE_ROWS(DD)                                                                                              \
+  qk_norm_rope_rows_kernel<DD><<<grid, 256, 0, st>>>(                                                                  \
+      (const __nv_bfloat16*)qkv, row_stride, q_head_stride, k_col, v_col, (const __nv_bfloat16*)q_norm_w,              \
+      (const __nv_bfloat16*)k_norm_w, eps, norm_plus_one, pos, inv, rotary_dim, (__nv_bfloat16*)q_out,                \
+      (__nv_bfloat16*)k_arena, (__nv_bfloat16*)v_arena, kv_row_stride, kv_rows, hq, hkv, n_tokens)
+    if (head_dim == 64) CEVK_ROPE_ROWS(64);
+    else if (head_dim == 128) CEVK_ROPE_ROWS(128);
+    else CEVK_ROPE_ROWS(256);
+#undef CEVK_ROPE_ROWS
+    return check_launch("qk_norm_rope_rows_kernel");
+  }
   if (vec && (dtype == CEVK_BF16 || dtype == CEVK_F32)) {
 #define CEVK_ROPE_VEC(TT, EE)                                                                                          \
   qk_norm_rope_vec_kernel<TT, EE><<<blocks, 256, 0, st>>>(                                                             \
