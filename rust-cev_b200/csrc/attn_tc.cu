@@ -8,22 +8,27 @@
 // token).  Key tiles of other segments are never loaded, and no mask is
 // materialised: validity is decided per element from the segment descriptor.
 //
-// A CTA runs NT work tiles (the launches use NT = 1 with two CTAs per SM
-// for head_dim 64 / 128, so one CTA's softmax overlaps the other's UMMAs;
-// one CTA per SM for head_dim 256).  With NT = 2 one UMMA issuer alternates
-// strictly between the tiles.  Warp roles (256 threads for NT = 1):
-//   warps 0 / 3   TMA producers for Q and K of tile 0 / 1 (one elected lane)
-//   warps 2 / 12  TMA producers for V of tile 0 / 1
-//   warp 1        TMEM allocator + UMMA issuer (one elected lane)
-//   warps 4-7 / 8-11  softmax / O correction / epilogue of tile 0 / 1, one
-//                 query row per thread (TMEM lane = row).
-// TMEM per tile: two S buffers (BN f32 columns each) so QK^T of block j+1
-// runs while block j is in softmax, and the O accumulator (D f32 columns).
-// P (bf16) overwrites its own S in TMEM and feeds the PV UMMA as the TMEM A
-// operand, so the softmax never waits for the previous PV (only an O
-// rescale does).  Online softmax in the log2 domain; O is only rescaled when
-// a row max grows by more than 2^8 (values of P stay <= 256, exact in f32
-// accumulation), which keeps TMEM traffic off the common path.
+// A CTA runs one work tile, two CTAs per SM for head_dim 64 / 128 (one
+// CTA's softmax overlaps the other's UMMAs), one per SM for head_dim 256.
+// Warp roles (256 threads):
+//   warp 0        TMA producer for Q and K (one lane)
+//   warp 2        TMA producer for V
+//   warp 1        TMEM allocator + issuer of the S = Q K^T UMMAs (one lane)
+//   warp 3        issuer of the O += P V UMMAs (one lane)
+//   warps 4-7     softmax / O correction / epilogue, one query row per
+//                 thread (TMEM lane = row).
+// The two UMMA streams only meet through the softmax (S_j -> P_j), so with
+// one issuing thread each a burst of one never queues behind the other's
+// issue (a tcgen05.mma takes tens of cycles to issue from one thread).
+// TMEM per tile: S (BN f32 columns), a double buffer for P (bf16 packed in
+// pairs, BN/2 columns each) and the O accumulator (D f32 columns).  S_{j+1}
+// is issued as soon as the softmax has S_j in registers, so it runs while
+// block j is in softmax; P_j feeds the PV UMMA as the TMEM A operand, and
+// the softmax only waits for PV_{j-2} before reusing its P buffer (and for
+// PV_{j-1} before an O rescale).  Online softmax in the log2 domain; O is
+// only rescaled when a row max grows by more than 2^8 (values of P stay
+// <= 256, exact in f32 accumulation), which keeps TMEM traffic off the
+// common path.
 //
 // Split-KV (n_split > 1): when the call has too few tiles to fill the GPU
 // (a prefill chunk after a long cached prefix), each tile's key blocks are
@@ -58,7 +63,7 @@ struct AttnTc {
   // most one phase away from its barrier; the comments at each wait say why.
   static constexpr int T_BARS = 1 + 2 * KSK + 2 * KSV + 6;
   static constexpr int OFF_BAR = NT * T_BYTES;
-  static constexpr int OFF_MISC = OFF_BAR + (NT * T_BARS + 1) * 8;  // + drain
+  static constexpr int OFF_MISC = OFF_BAR + (NT * T_BARS + 2) * 8;  // + drain of the S and PV issuers
   static constexpr int SMEM = OFF_MISC + 16;
   // TMEM per tile: S (BN f32 columns), P double buffer (BN/2 columns of
   // packed bf16 each), O (D f32 columns).
@@ -176,7 +181,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   auto b_sfree = [&](int t) { return bar(t, 2 + KV4); };
   auto b_pfull = [&](int t, int s) { return bar(t, 3 + KV4 + s); };
   auto b_odone = [&](int t, int s) { return bar(t, 5 + KV4 + s); };
-  const uint32_t b_drain = sbase + C::OFF_BAR + 8u * (NT * C::T_BARS);
+  const uint32_t b_drain_s = sbase + C::OFF_BAR + 8u * (NT * C::T_BARS);
+  const uint32_t b_drain_o = b_drain_s + 8u;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
@@ -200,7 +206,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       mbar_init(b_odone(t, 0), 1);
       mbar_init(b_odone(t, 1), 1);
     }
-    mbar_init(b_drain, 1);
+    mbar_init(b_drain_s, 1);
+    mbar_init(b_drain_o, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -213,10 +220,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Roles: warp 0 / 3 load Q and K of tile 0 / 1, warp 2 / 12 load V of
-  // tile 0 / 1, warp 1 issues UMMAs, warps 4-7 / 8-11 run tile 0 / 1's softmax.
-  const int qk_tile = warp == 0 ? 0 : (NT == 2 && warp == 3 ? 1 : -1);
-  const int v_tile = warp == 2 ? 0 : (NT == 2 && warp == 12 ? 1 : -1);
+  // Roles: warp 0 loads Q and K, warp 2 loads V, warps 1 / 3 issue the S /
+  // PV UMMAs, warps 4-7 run the softmax.
+  static_assert(NT == 1, "one work tile per CTA");
+  const int qk_tile = warp == 0 ? 0 : -1;
+  const int v_tile = warp == 2 ? 0 : -1;
 
   if (qk_tile >= 0 && lane == 0) {
     // ---------------- Q + K producer of one tile ----------------
@@ -265,73 +273,62 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       for (int j = max(0, issued - KSV); j < issued; ++j)
         mbar_wait(b_vfull(t, j % KSV), (j / KSV) & 1, &never, 1ll << 30);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- UMMA issuer, alternating between the tiles ----------------
-    constexpr uint32_t idesc_s = umma_idesc_bf16(128, BN, 0, 0);
-    constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 0, 1);
-    int nb[NT];
-    bool ok = true, issued_any = false;
+  } else if ((warp == 1 || warp == 3) && lane == 0) {
+    // ---------------- UMMA issuers ----------------
+    // Warp 1 issues S = Q K^T, warp 3 issues O += P V.  The two streams only
+    // meet through the softmax (S_j -> P_j), so a burst of one never waits
+    // behind the other's issue; each thread commits and drains its own UMMAs.
+    constexpr int t = 0;
+    const int nb = decode_work(p, blockIdx.x, BN).n_blk;
+    bool ok = nb > 0, issued_any = false;
+    if (warp == 1) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, BN, 0, 0);
+      if (ok) ok = mbar_wait(b_qfull(t), 0, abort_flag);
+      for (int j = 0; ok && j < nb; ++j) {
+        // S_j as soon as the softmax has S_{j-1} in registers: it runs on
+        // the tensor cores while the softmax computes block j-1.  (s_free
+        // cannot lead this wait by two phases: the softmax only loads S_j
+        // after this thread issued it.)
+        if (j > 0 && !mbar_wait(b_sfree(t), (j - 1) & 1, abort_flag)) break;
+        const int st = j % KSK;
+        if (!mbar_wait(b_kfull(t, st), (j / KSK) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + C::TM_S;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      nb[t] = decode_work(p, blockIdx.x * NT + t, BN).n_blk;
-      if (nb[t] > 0 && ok) ok = mbar_wait(b_qfull(t), 0, abort_flag);
-    }
-    auto issue_s = [&](int t, int j) -> bool {
-      const int st = j % KSK;
-      if (!mbar_wait(b_kfull(t, st), (j / KSK) & 1, abort_flag)) return false;
-      tc_fence_after();
-      const uint32_t d = tmem + t * C::TM_TILE + C::TM_S;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint64_t ad = umma_desc_sw128(sQ(t) + (kk >> 2) * C::ATOM + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = umma_desc_sw128(sK(t, st) + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-        umma_bf16_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(sQ(t) + (kk >> 2) * C::ATOM + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(sK(t, st) + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(b_sfull(t));
+        umma_commit(b_kempty(t, st));
+        issued_any = true;
       }
-      umma_commit(b_sfull(t));
-      umma_commit(b_kempty(t, st));
-      issued_any = true;
-      return true;
-    };
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-      if (ok && nb[t] > 0) ok = issue_s(t, 0);
-    int nmax = 0;
-#pragma unroll
-    for (int t = 0; t < NT; ++t) nmax = max(nmax, nb[t]);
-    for (int j = 0; ok && j < nmax; ++j) {
-      // S_{j+1} as soon as the softmax has S_j in registers: it runs on the
-      // tensor cores while the softmax computes block j.  (s_free cannot
-      // lead this wait by two phases: the softmax only loads S_{j+1} after
-      // this issue.)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (!ok || j + 1 >= nb[t]) continue;
-        if (!mbar_wait(b_sfree(t), j & 1, abort_flag)) { ok = false; break; }
-        ok = issue_s(t, j + 1);
-      }
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (!ok || j >= nb[t]) continue;
+    } else {
+      constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 0, 1);
+      for (int j = 0; ok && j < nb; ++j) {
         // p_full[j&1] cannot lead by two phases: P_{j+2} is only written
         // after PV_j (issued right below) completed.
-        if (!mbar_wait(b_pfull(t, j & 1), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(b_pfull(t, j & 1), (j >> 1) & 1, abort_flag)) break;
         const int st = j % KSV;
-        if (!mbar_wait(b_vfull(t, st), (j / KSV) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(b_vfull(t, st), (j / KSV) & 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t pa = tmem + t * C::TM_TILE + C::TM_P + (j & 1) * (BN / 2);
+        const uint32_t pa = tmem + C::TM_P + (j & 1) * (BN / 2);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bd = umma_desc_sw128(sV(t, st) + kk * 16 * 128, BN * 128, 1024);
-          umma_bf16_ts(tmem + t * C::TM_TILE + C::TM_O, pa + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + C::TM_O, pa + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(b_odone(t, j & 1));
         umma_commit(b_vempty(t, st));
+        issued_any = true;
       }
     }
     // Every UMMA this thread issued has completed before TMEM is freed
     // (an item with no key blocks -- a key range past its tile's last --
     // issued none).
     if (issued_any) {
+      const uint32_t b_drain = warp == 1 ? b_drain_s : b_drain_o;
       umma_commit(b_drain);
       volatile int never = 0;
       mbar_wait(b_drain, 0, &never, 1ll << 30);
@@ -352,7 +349,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     for (int j = 0; j < wk.n_blk; ++j) {
       // s_full cannot lead by two phases: S_{j+1} is only issued after this
       // thread released S_j through s_free.
-      if (!mbar_wait(b_sfull(t), j & 1, abort_flag)) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(b_sfull(t), j & 1, abort_flag))) { ok = false; break; }
       tc_fence_after();
       const uint32_t sc = tl + C::TM_S;
 #pragma unroll
@@ -406,13 +403,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // behind by a phase (PV_{j-4} was waited here two blocks ago) nor
       // ahead (PV_j needs P_j).
       if (j >= 2) {
-        if (!mbar_wait(b_odone(t, j & 1), ((j - 2) >> 1) & 1, abort_flag)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(b_odone(t, j & 1), ((j - 2) >> 1) & 1, abort_flag))) { ok = false; break; }
         tc_fence_after();
       }
       if (__any_sync(0xffffffffu, factor != 1.f)) {
         // O is rescaled in TMEM: PV of the previous block must be done (and
         // PV of this block cannot start before P_j is signalled).
-        if (!mbar_wait(b_odone(t, (j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(b_odone(t, (j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag))) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D; c += 32) {
@@ -435,7 +432,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int vcount = (jg < wk.n_pre) ? wk.seg.prefix_len - jg * BN : own_rows - (jg - wk.n_pre) * BN;
         if (vcount < BN) {
           const int vst = j % KSV;
-          if (!mbar_wait(b_vfull(t, vst), (j / KSV) & 1, abort_flag)) { ok = false; break; }
+          if (!__all_sync(0xffffffffu, mbar_wait(b_vfull(t, vst), (j / KSV) & 1, abort_flag))) { ok = false; break; }
           const int rows0 = vcount < 0 ? 0 : vcount;
           const int chunks = (BN - rows0) * 8 * (D / 64);
           uint8_t* vb = smem + t * C::T_BYTES + C::T_OFF_V + vst * C::KV_BYTES;

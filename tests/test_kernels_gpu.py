@@ -70,6 +70,11 @@ CASES = [
     (16, 4, 256, [(0, 128, 0, 1000, 1000)], 128, 1128),
     (32, 8, 64, [(0, 64, 0, 700, 700), (64, 3, 0, 700, 764)], 67, 767),
     (8, 8, 128, [(0, 200, 0, 0, 0)], 200, 200),
+    # head_dim 64, one and two heads per KV head: a 128-row tile spans two
+    # own key blocks, so the odd block (the second softmax group's) is fully
+    # masked for half the rows; one-block segments leave that group idle
+    (4, 4, 64, [(0, 300, 0, 0, 0)], 300, 300),
+    (8, 4, 64, [(0, 5, 0, 0, 0), (5, 130, 0, 70, 135), (135, 64, 70, 1, 265)], 199, 329),
 ]
 
 
@@ -98,7 +103,7 @@ def test_attention_f32_matches_oracle(case):
     assert (out.cpu()[rows] - want[rows]).abs().max().item() < F32_TOL
 
 
-@pytest.mark.parametrize("case", [1, 2, 5])
+@pytest.mark.parametrize("case", [1, 2, 5, 7, 8])
 def test_attention_ignores_nonfinite_rows_outside_segments(case):
     """Rows of K/V outside every segment's visible range may hold anything
     (NaN/Inf garbage of an uninitialised arena): outputs stay exact."""
@@ -367,6 +372,7 @@ SPLIT_CASES = [
     (16, 8, 128, [(0, 64, 0, 2048, 2048), (64, 100, 0, 65, 2112), (164, 40, 0, 0, 2212)], 204, 2252),
     (16, 4, 256, [(0, 128, 0, 1000, 1000)], 128, 1128),
     (2, 1, 128, [(0, 37, 0, 100, 300), (37, 150, 0, 100, 337), (187, 5, 100, 0, 487)], 192, 492),
+    (2, 2, 64, [(0, 256, 0, 1900, 2000), (256, 3, 0, 130, 2256)], 259, 2259),
 ]
 
 
@@ -396,11 +402,12 @@ def test_attention_split_kv_matches_oracle(case, n_split):
             assert (out[qs:qs + ql].float().cpu() - want[0].transpose(0, 1)).abs().max().item() < BF16_TOL
 
 
-def test_attention_split_kv_ignores_nonfinite_rows():
+@pytest.mark.parametrize("case", [2, 5])
+def test_attention_split_kv_ignores_nonfinite_rows(case):
     """Split ranges load only visible K/V rows: NaN/Inf elsewhere in the
     arena leaves the output bits unchanged."""
     from cev_b200 import ops
-    hq, hkv, D, segs, n_tok, n_kv = SPLIT_CASES[2]
+    hq, hkv, D, segs, n_tok, n_kv = SPLIT_CASES[case]
     q, k, v = rand_attn(n_tok, n_kv, hq, hkv, D, torch.bfloat16, 450)
     used = torch.zeros(n_kv, dtype=torch.bool)
     for (qs, ql, po, pl, so) in segs:
