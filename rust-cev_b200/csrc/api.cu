@@ -153,15 +153,37 @@ int cevk_attn_split_plan(const cevk_segment* segs, int32_t n_segs, int32_t n_til
   *n_split = 1;
   *workspace_bytes = 0;
   if (dtype != CEVK_BF16 || n_segs <= 0 || n_tiles <= 0 || hkv <= 0 || n_sms <= 0) return CEVK_OK;
-  // One wave: two resident CTAs per SM for head_dim <= 128, one for 256.
+  // Resident CTAs: two per SM for head_dim <= 128, one for 256.
   const int64_t slots = (int64_t)n_sms * (head_dim <= 128 ? 2 : 1);
   const int64_t n_work = (int64_t)n_tiles * hkv;
-  int max_pre = 0;
-  for (int i = 0; i < n_segs; ++i) max_pre = std::max(max_pre, (segs[i].prefix_len + 63) / 64);
-  // Split while the items still fit one wave and every range keeps at
-  // least 8 key blocks (512 keys) to amortise its Q load and epilogue.
-  int64_t s = std::min<int64_t>({slots / n_work, (int64_t)max_pre / 8, 32});
-  if (s < 2 || n_work * s >= (1ll << 30)) return CEVK_OK;
+  int max_pre = 0, max_total = 0;
+  for (int i = 0; i < n_segs; ++i) {
+    max_pre = std::max(max_pre, (segs[i].prefix_len + 63) / 64);
+    max_total = std::max(max_total, (segs[i].prefix_len + segs[i].q_len + 63) / 64);
+  }
+  // Cost model in 64-key blocks: a CTA item of b blocks costs b + kFix
+  // (its Q load, first S and epilogue, about three block periods measured),
+  // and equal items run in waves of `slots`.  Take the split count with the
+  // lowest waves x (blocks per range + kFix), at least 8 blocks (512 keys)
+  // per range, and only when it saves 3% over fewer ranges (the merge
+  // reads every range's rows once more).  Wave quantisation is what the
+  // count trades against: 128 items on 296 slots fill 86% of one wave,
+  // 1152 items fill 97% of four.
+  constexpr int64_t kFix = 3;
+  auto cost = [&](int64_t s) {
+    const int64_t waves = (n_work * s + slots - 1) / slots;
+    return waves * ((max_total + s - 1) / s + kFix);
+  };
+  int64_t s = 1, best = cost(1);
+  const int64_t s_max = std::min<int64_t>((int64_t)max_pre / 8, 32);
+  for (int64_t c = 2; c <= s_max && n_work * c < (1ll << 30); ++c) {
+    const int64_t k = cost(c);
+    if (k * 100 < best * 97) {
+      best = k;
+      s = c;
+    }
+  }
+  if (s < 2) return CEVK_OK;
   *n_split = (int32_t)s;
   *workspace_bytes = cevk_attn_split_workspace_size(n_tiles, hkv, head_dim, (int32_t)s);
   return CEVK_OK;
