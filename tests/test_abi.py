@@ -85,15 +85,18 @@ def _plan(rows, n_tok, n_kv, hq, hkv, D, sms=148):
     return n.value, ns.value, nb.value
 
 
-def test_split_plan_fills_one_wave_of_underfilled_calls():
+def test_split_plan_fills_the_waves_of_underfilled_calls():
     """A 512-token prefill chunk after a long prefix (cfg5's LFM2 chunk:
     32 Q / 8 KV heads, head_dim 64 -> 16 tiles x 8 KV heads = 128 CTAs on
-    148 SMs x 2) splits in two; one KV head per rank (the 8-way KV-head
-    split) splits 18 ways; a short prefix or an already full call does not
-    split; the workspace is one f32 row + log-sum-exp per range and row."""
+    148 SMs x 2) splits 9 ways (1152 items fill 97% of four waves; 2 ranges
+    would fill 86% of one) after 32768 tokens and 2 ways after 8192; one KV
+    head per rank (the 8-way KV-head split) splits 18 ways; a short prefix
+    or an already full call does not split; the workspace is one f32 row +
+    log-sum-exp per range and row."""
     lib = _lib.lib()
     tiles, ns, nb = _plan([(0, 512, 0, 32768, 32768)], 512, 33280, 32, 8, 64)
-    assert (tiles, ns) == (16, 2) and nb == 16 * 8 * 2 * 128 * 65 * 4
+    assert (tiles, ns) == (16, 9) and nb == 16 * 8 * 9 * 128 * 65 * 4
+    assert _plan([(0, 512, 0, 8192, 8192)], 512, 8704, 32, 8, 64)[1] == 2
     assert nb == lib.cevk_attn_split_workspace_size(tiles, 8, 64, ns)
     assert _plan([(0, 512, 0, 32768, 32768)], 512, 33280, 4, 1, 64)[1] == 18
     assert _plan([(0, 512, 0, 448, 448)], 512, 960, 4, 1, 64)[1] == 1        # 7 prefix blocks: too short
