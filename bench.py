@@ -490,8 +490,9 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     del w
     codes = workloads.code_ids(4)
     # cfg4's state is run once: one 16384-token pass; cfg5's is prefilled in 512-token chunks
+    # cfg5's 128 state chunks on one GPU replay from CUDA graphs
     eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=plen if name == "cfg4" else 512, pass_tokens=8192,
-                              prefix_cache_tokens=plen)
+                              prefix_cache_tokens=plen, chunk_graphs=name == "cfg5" and split is None)
     vocab = cfg["vocab_size"] - 1
     stream = 0 if split is not None else rank  # a split model runs the same requests on every rank
     reqs = [workloads.decision_request(20_000 * (stream + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]

@@ -35,6 +35,9 @@ class HybridState:
     next_pos: int = 0
     gdn: dict = field(default_factory=dict)    # layer -> (conv tail [1,C,K-1], S [1,nv,dk,dv] f32)
     conv: dict = field(default_factory=dict)   # layer -> tail [1,d,K-1]
+    # token split over ranks: the rank whose conv tails are current (it ran
+    # the sequence's last token), or -1 when every rank's are
+    tail_rank: int = -1
     pins: int = 0
     released: bool = False
 
@@ -104,27 +107,102 @@ class _HybridDecoder:
             rows_t = torch.tensor(rows, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
             plan = ops.AttnPlan(segs, n, self.arena.capacity, self.hq_a, self.hkv_a, self.D, self.dtype, dev)
         try:
-            x = ops.embed(self.embed_w, ids)
-            h = ops.rms_norm(x, self.layers[0]["ln1"], self.eps, self.plus_one)
-            m = None
-            for i, L in enumerate(self.layers):
-                if m is not None:
-                    h = ops.add_rms_norm(x, m, L["ln1"], self.eps, self.plus_one, out=h)
-                if L["kind"] == "attn":
-                    o = self._attn(i, L, h, pos_t, rows_t, plan)
-                elif L["kind"] == "gdn":
-                    o = self._gdn(i, L, h, B, T, state, keep)
-                else:
-                    o = self._conv(i, L, h, B, T, state, keep)
-                h = ops.add_rms_norm(x, o, L["ln2"], self.eps, self.plus_one, out=h)
-                m = F.linear(ops.swiglu(F.linear(h, L["gu"])), L["down"])
-            ops.residual_add(x, m)
+            if self._token_split(B, T):
+                x = self._layers_token_split(ids, B, T, pos_t, rows_t, plan, state, keep)
+            else:
+                if self.split is not None and state is not None and state.tail_rank >= 0:
+                    self._share_tails(state)
+                x = ops.embed(self.embed_w, ids)
+                h = ops.rms_norm(x, self.layers[0]["ln1"], self.eps, self.plus_one)
+                m = None
+                for i, L in enumerate(self.layers):
+                    if m is not None:
+                        h = ops.add_rms_norm(x, m, L["ln1"], self.eps, self.plus_one, out=h)
+                    if L["kind"] == "attn":
+                        o = self._attn(i, L, h, pos_t, rows_t, plan)
+                    elif L["kind"] == "gdn":
+                        o = self._gdn(i, L, h, B, T, state, keep)
+                    else:
+                        o = self._conv(i, L, h, B, T, state, keep)
+                    h = ops.add_rms_norm(x, o, L["ln2"], self.eps, self.plus_one, out=h)
+                    m = F.linear(ops.swiglu(F.linear(h, L["gu"])), L["down"])
+                ops.residual_add(x, m)
         finally:
             if scratch is not None:
                 self.arena.release(scratch, n)
         if keep:
             state.len = past + T
             state.next_pos = max(pos) + 1
+        return x
+
+    def _token_split(self, B, T) -> bool:
+        """Token-local layers split over the ranks of a KV-head split: a row
+        batch by whole rows, a sequence chunk by contiguous runs of at least
+        K-1 tokens (shorter chunks run whole on every rank)."""
+        sp = self.split
+        if sp is None or sp.world < 2 or not sp.sequence_parallel:
+            return False
+        return B > 1 or T >= sp.world * max(getattr(self, "K", 1) - 1, 1)
+
+    def _share_tails(self, state):
+        """Every rank takes the short-conv tails of the rank that ran the
+        sequence's last token (one broadcast per conv layer, in layer order
+        on every rank)."""
+        for i, L in enumerate(self.layers):
+            if L["kind"] != "conv":
+                continue
+            t = state.conv.get(i)
+            if t is None:
+                t = state.conv[i] = torch.zeros(1, self.hidden, self.K - 1, dtype=self.dtype, device=self.device)
+            self.split.broadcast(t, state.tail_rank)
+        state.tail_rank = -1
+
+    def _layers_token_split(self, ids, B, T, pos_t, rows_t, plan, state, keep):
+        """The layer loop with a KV-head split over ranks: attention runs
+        this rank's heads on every token (its head outputs gathered across
+        ranks), everything token-local -- the output projection, the short
+        conv, the MLP, the norms -- runs only on this rank's token rows, and
+        one all-gather per layer rebuilds the residual stream on every rank.
+        A row batch splits by whole rows (each continues the state's conv
+        tails, shared first).  A sequence chunk splits into contiguous runs,
+        the first run on the rank holding the conv tails; a later run's
+        short conv also runs over the K-1 tokens before it (their outputs
+        are dropped), and the rank that runs the chunk's last token keeps
+        the new tails."""
+        sp = self.split
+        n = B * T
+        if B > 1:
+            if state is not None and state.tail_rank >= 0:
+                self._share_tails(state)
+            per = -(-B // sp.world)
+            a, b, unit = min(B, sp.rank * per) * T, min(B, (sp.rank + 1) * per) * T, per * T
+            runs = None
+        else:
+            unit = -(-T // sp.world)
+            first = 0 if state is None or state.tail_rank < 0 else state.tail_rank
+            runs = [(r - first) % sp.world for r in range(sp.world)]  # run index of each rank
+            a, b = min(T, runs[sp.rank] * unit), min(T, (runs[sp.rank] + 1) * unit)
+        x = ops.embed(self.embed_w, ids)
+        for i, L in enumerate(self.layers):
+            if L["kind"] == "attn":
+                h = ops.rms_norm(x, L["ln1"], self.eps, self.plus_one)
+                ctx = self._attn_ctx(i, L, h, pos_t, rows_t, plan)
+                o = F.linear(ctx[a:b], L["o"]) if b > a else None
+            elif L["kind"] == "conv":
+                o = self._conv_rows(i, L, x, a, b, B, T, state, keep)
+            else:
+                raise NotImplementedError("token split: attention and short-conv layers only")
+            if b > a:
+                xs = x[a:b]
+                hs = ops.add_rms_norm(xs, o, L["ln2"], self.eps, self.plus_one)
+                ops.residual_add(xs, F.linear(ops.swiglu(F.linear(hs, L["gu"])), L["down"]))
+            if runs is None:
+                sp.gather_rows(x, a, b, unit)
+            else:
+                sp.gather_runs(x, a, b, unit, runs)
+        if keep and runs is not None:
+            last = (T - 1) // unit
+            state.tail_rank = runs.index(last)
         return x
 
     def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot, attend=None):
@@ -249,19 +327,22 @@ class Lfm2(_HybridDecoder):
             self.layers.append(L)
         self.norm_w = w("model.embedding_norm.weight")
 
-    def _attn(self, i, L, h, pos_t, rows_t, plan):
-        """lfm2.rs:145-171; with a KV-head split, this rank's heads and one
-        all-gather of the head outputs before the output projection."""
+    def _attn_ctx(self, i, L, h, pos_t, rows_t, plan):
+        """lfm2.rs:145-171 up to the output projection: the attention output
+        of every head, [T, Hq * D]; with a KV-head split, this rank's heads
+        and one all-gather of the head outputs (or the gather fused into the
+        attention epilogue)."""
         hq, hkv, D = self.hq_a, self.hkv_a, self.D
         fused = self.split.fused if self.split is not None else None
         _, ctx = self._attn_common(i, L, h, pos_t, rows_t, plan, (0, D), hq * D, (hq + hkv) * D, D,
                                    attend=None if fused is None else fused.attend)
         if fused is not None:  # already gathered by the attention epilogue
-            return F.linear(ctx, L["o"])
+            return ctx
         ctx = ctx.view(h.shape[0], hq * D)
-        if self.split is not None:
-            ctx = self.split.gather(ctx)
-        return F.linear(ctx, L["o"])
+        return ctx if self.split is None else self.split.gather(ctx)
+
+    def _attn(self, i, L, h, pos_t, rows_t, plan):
+        return F.linear(self._attn_ctx(i, L, h, pos_t, rows_t, plan), L["o"])
 
     def _conv(self, i, L, h, B, T, state, keep):
         """ShortConv::forward (lfm2.rs:199-219)."""
@@ -274,14 +355,175 @@ class Lfm2(_HybridDecoder):
             state.conv[i] = tail_out
         return F.linear(y, L["out"])
 
+    def _conv_rows(self, i, L, x, a, b, B, T, state, keep):
+        """ShortConv::forward (lfm2.rs:199-219) on token rows [a, b) of the
+        residual stream x [B*T, H]: whole rows continuing the state's tails
+        (B > 1), or a run of one sequence, computed over the K-1 tokens
+        before it too (its first K-1 outputs are dropped) unless it starts
+        the sequence, where the state's tails precede it.  The run holding
+        the sequence's last token writes the new tails."""
+        d, K = self.hidden, self.K
+        tail_prev = None if state is None else state.conv.get(i)
+        if b <= a:
+            return None
+        if B > 1:
+            bcx = F.linear(ops.rms_norm(x[a:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+            y = ops.short_conv(bcx, (b - a) // T, T, d, L["conv_w"], L["bias"], tail_prev, None)
+            return F.linear(y, L["out"])
+        lo = max(0, a - (K - 1))
+        tail_out = None
+        if keep and b == T:
+            tail_out = torch.empty(1, d, K - 1, dtype=self.dtype, device=self.device)
+        bcx = F.linear(ops.rms_norm(x[lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+        y = ops.short_conv(bcx, 1, b - lo, d, L["conv_w"], L["bias"], tail_prev if a == 0 else None, tail_out)
+        if tail_out is not None:
+            state.conv[i] = tail_out
+        return F.linear(y[a - lo:], L["out"])
+
+
+class ChunkGraphs:
+    """The full-size prefill chunks of an LFM2 decoder (short-conv and
+    attention layers, one GPU) replayed from CUDA graphs.
+
+    A 512-token chunk of the cfg5 state is ~150 kernel launches whose host
+    cost (Python, torch dispatch, ctypes) rivals their device time; a graph
+    replays them with one launch.  Everything a chunk varies lives in
+    device memory the graph reads: the token ids, positions and arena rows,
+    the attention segment (its prefix length grows chunk by chunk), and the
+    short-conv tails, which alternate between two static buffers (a chunk
+    reads one and writes the other).  What changes the launches themselves
+    -- the split-KV range count the planner picks for the prefix length,
+    and which tail buffer is read -- selects the graph, captured on first
+    use after one eager run of the same chunk (the chunk is idempotent: it
+    rewrites the same K/V rows and tails).  After the last graph chunk the
+    state's tails are copied out of the static buffers."""
+
+    def __init__(self, dec: "Lfm2", T: int):
+        from ._lib import Segment
+        if dec.split is not None or any(L["kind"] not in ("conv", "attn") for L in dec.layers):
+            raise ValueError("chunk graphs: one-GPU LFM2 decoders only")
+        self.dec, self.T = dec, T
+        dev = dec.device
+        # pinned staging ring: a slot is rewritten only after its copy ran
+        self.host = [torch.empty(3 * T + 7, dtype=torch.int32).pin_memory() for _ in range(4)]
+        self.copied = [None] * len(self.host)
+        self.slot = 0
+        self.inputs = torch.zeros(3 * T + 7, dtype=torch.int32, device=dev)
+        self.ids, self.pos, self.rows = self.inputs[:T], self.inputs[T:2 * T], self.inputs[2 * T:3 * T]
+        self.seg = self.inputs[3 * T:]
+        self.conv_layers = [i for i, L in enumerate(dec.layers) if L["kind"] == "conv"]
+        self.tails = [{i: torch.zeros(1, dec.hidden, dec.K - 1, dtype=dec.dtype, device=dev)
+                       for i in self.conv_layers} for _ in range(2)]
+        self.graphs = {}
+        self.pool = torch.cuda.graph_pool_handle()
+        self.sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self._seg_t = Segment
+
+    def _split_count(self, seg) -> int:
+        """Split-KV range count the planner picks for this chunk's segment
+        (host only)."""
+        import ctypes as C
+
+        from ._lib import BF16, F32, check, lib
+        dec = self.dec
+        arr = (self._seg_t * 1)()
+        arr[0].q_start, arr[0].q_len, arr[0].prefix_off, arr[0].prefix_len, arr[0].self_off = seg
+        dt = BF16 if dec.dtype == torch.bfloat16 else F32
+        tiles, ns, nb = C.c_int32(0), C.c_int32(1), C.c_int64(0)
+        check(lib().cevk_attn_schedule(arr, 1, self.T, dec.arena.capacity, dec.hq_a, dec.hkv_a, dec.D, dt,
+                                       C.byref(tiles)))
+        check(lib().cevk_attn_split_plan(arr, 1, tiles.value, dec.hkv_a, dec.D, dt, self.sms, C.byref(ns),
+                                         C.byref(nb)))
+        return ns.value if dt == BF16 else 1
+
+    def _body(self, plan, parity: int):
+        dec, T = self.dec, self.T
+        rd, wr = self.tails[parity], self.tails[1 - parity]
+        x = ops.embed(dec.embed_w, self.ids)
+        h = ops.rms_norm(x, dec.layers[0]["ln1"], dec.eps, dec.plus_one)
+        m = None
+        for i, L in enumerate(dec.layers):
+            if m is not None:
+                h = ops.add_rms_norm(x, m, L["ln1"], dec.eps, dec.plus_one, out=h)
+            if L["kind"] == "attn":
+                o = dec._attn(i, L, h, self.pos, self.rows, plan)
+            else:
+                y = ops.short_conv(F.linear(h, L["in_proj"]), 1, T, dec.hidden, L["conv_w"], L["bias"], rd[i], wr[i])
+                o = F.linear(y, L["out"])
+            h = ops.add_rms_norm(x, o, L["ln2"], dec.eps, dec.plus_one, out=h)
+            m = F.linear(ops.swiglu(F.linear(h, L["gu"])), L["down"])
+        ops.residual_add(x, m)
+        return x
+
+    def run(self, tokens, state: HybridState, parity: int) -> None:
+        """One T-token chunk continuing ``state`` (keep): reads the tails in
+        buffer ``parity``, writes the other."""
+        dec, T = self.dec, self.T
+        past = state.len
+        base = state.start + past
+        p0 = state.next_pos
+        seg = (0, T, state.start, past, base)
+        k = self.slot
+        self.slot = (k + 1) % len(self.host)
+        if self.copied[k] is not None:
+            self.copied[k].synchronize()
+        host = self.host[k]
+        host[:T] = torch.as_tensor(tokens, dtype=torch.int32)
+        host[T:2 * T] = torch.arange(p0, p0 + T, dtype=torch.int32)
+        host[2 * T:3 * T] = torch.arange(base, base + T, dtype=torch.int32)
+        host[3 * T:] = torch.tensor([*seg, 0, 0], dtype=torch.int32)  # tile_start 0, flags 0
+        self.inputs.copy_(host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.copied[k] = ev
+        for i in self.conv_layers:
+            cur = state.conv.get(i)
+            if cur is None:
+                self.tails[parity][i].zero_()
+            elif cur.data_ptr() != self.tails[parity][i].data_ptr():
+                self.tails[parity][i].copy_(cur)
+        n_split = self._split_count(seg)
+        key = (n_split, parity)
+        entry = self.graphs.get(key)
+        if entry is None:
+            plan = ops.AttnPlan([seg], T, dec.arena.capacity, dec.hq_a, dec.hkv_a, dec.D, dec.dtype, dec.device,
+                                n_split=n_split)
+            plan.dev = self.seg  # the launches read the segment from the static inputs
+            cur = torch.cuda.current_stream(dec.device)
+            side = torch.cuda.Stream(device=dec.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self._body(plan, parity)
+            cur.wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.pool):
+                self._body(plan, parity)
+            entry = self.graphs[key] = (g, plan)
+        entry[0].replay()
+        for i in self.conv_layers:
+            state.conv[i] = self.tails[1 - parity][i]
+        state.len = past + T
+        state.next_pos = p0 + T
+
+    def release_tails(self, state: HybridState) -> None:
+        """Give the state its own copies of tails that live in the static
+        buffers (the next chunk or request overwrites those)."""
+        for i in self.conv_layers:
+            t = state.conv.get(i)
+            if t is not None and any(t.data_ptr() == b[i].data_ptr() for b in self.tails):
+                state.conv[i] = t.clone()
+
 
 class HybridEngine:
     """Codes readout of the hybrid engine (hybrid.rs:155-165, 454-772)."""
 
     def __init__(self, decoder: _HybridDecoder, code_ids, pad_id: int, prefill_chunk=512, pass_tokens=2048,
-                 prefix_cache_tokens=65536, device_readout=False):
+                 prefix_cache_tokens=65536, device_readout=False, chunk_graphs=False):
+        """``chunk_graphs``: replay the full-size prefill chunks of a
+        one-GPU LFM2 decoder from CUDA graphs (:class:`ChunkGraphs`)."""
         self.device_readout = device_readout  # readouts stay on the device (on-device debias)
         self.decoder = decoder
+        self.graphs = ChunkGraphs(decoder, prefill_chunk) if chunk_graphs else None
         self.head = decoder.head_rows(code_ids).contiguous()
         self.pad_id = pad_id
         self.prefill_chunk = prefill_chunk
@@ -293,12 +535,19 @@ class HybridEngine:
         chunk = max(self.prefill_chunk, 1)
         st = self.decoder.new_state(len(prefix), self.cache)
         st.pins += 1
+        graphs = getattr(self, "graphs", None)
         try:
-            done = 0
+            done, k = 0, 0
             while done < len(prefix):
                 n = min(chunk, len(prefix) - done)
-                self.decoder.forward(prefix[done:done + n], 1, n, range(done, done + n), st, True, self.cache)
+                if graphs is not None and n == chunk:
+                    graphs.run(prefix[done:done + n], st, k & 1)
+                    k += 1
+                else:
+                    self.decoder.forward(prefix[done:done + n], 1, n, range(done, done + n), st, True, self.cache)
                 done += n
+            if graphs is not None:
+                graphs.release_tails(st)
         except BaseException:
             st.pins -= 1
             st.release()

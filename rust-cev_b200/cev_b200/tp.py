@@ -27,6 +27,11 @@ class KvHeadSplit:
         self.hq_l, self.hkv_l = hq // world, hkv // world
         self.q0, self.kv0 = rank * self.hq_l, rank * self.hkv_l
         self.fused = None  # a FusedHeadGather once enable_fused_gather ran
+        # token-local layers on this rank's token rows only, the residual
+        # stream all-gathered after each layer (False: every rank runs them
+        # on every token)
+        self.sequence_parallel = False
+        self._run_index = {}
 
     def enable_fused_gather(self, max_tokens: int, device) -> "FusedHeadGather":
         """Gather head outputs from the attention epilogue over NVLink peer
@@ -44,6 +49,53 @@ class KvHeadSplit:
         k = w[k0:k0 + self.hkv_l * D]
         v = w[v0:v0 + self.hkv_l * D]
         return torch.cat([q, k, v], 0).contiguous()
+
+    def gather_rows(self, x: torch.Tensor, a: int, b: int, unit: int) -> None:
+        """x [n, H]: every rank r's rows [r * unit, min(n, (r + 1) * unit)),
+        this rank's being [a, b), gathered into x on every rank (one
+        all-gather; in place when n = world * unit)."""
+        n, H = x.shape
+        if n == self.world * unit and x.is_cuda:  # NCCL gathers in place
+            dist.all_gather_into_tensor(x, x[a:b], group=self.group)
+            return
+        send = x.new_zeros(unit, H)
+        send[:b - a] = x[a:b]
+        out = x.new_empty(self.world * unit, H)
+        dist.all_gather_into_tensor(out, send, group=self.group)
+        x.copy_(out[:n])
+
+    def gather_runs(self, x: torch.Tensor, a: int, b: int, unit: int, runs) -> None:
+        """Like :meth:`gather_rows` for a sequence whose runs are assigned
+        by rotation: rank r holds run ``runs[r]`` (rows [runs[r] * unit,
+        ...)), this rank's being [a, b)."""
+        if all(runs[r] == r for r in range(self.world)):
+            self.gather_rows(x, a, b, unit)
+            return
+        n, H = x.shape
+        flat = x.new_empty(self.world * unit, H)
+        if b - a == unit:
+            dist.all_gather_into_tensor(flat, x[a:b], group=self.group)
+        else:
+            send = x.new_zeros(unit, H)
+            send[:b - a] = x[a:b]
+            dist.all_gather_into_tensor(flat, send, group=self.group)
+        out = flat.view(self.world, unit, H)
+        if n == self.world * unit:
+            key = (tuple(runs), x.device)
+            idx = self._run_index.get(key)
+            if idx is None:
+                idx = self._run_index[key] = torch.tensor(runs, device=x.device)
+            x.view(self.world, unit, H).index_copy_(0, idx, out)
+            return
+        for r in range(self.world):
+            lo = runs[r] * unit
+            hi = min(n, lo + unit)
+            if hi > lo and r != self.rank:
+                x[lo:hi] = out[r, :hi - lo]
+
+    def broadcast(self, t: torch.Tensor, src: int) -> None:
+        """t from rank ``src`` to every rank, in place."""
+        dist.broadcast(t, src, group=self.group)
 
     def gather(self, ctx: torch.Tensor) -> torch.Tensor:
         """``[T, Hq/world * D]`` per rank -> ``[T, Hq * D]`` in head order

@@ -236,3 +236,36 @@ def test_run_many_batched_prefill_matches_one_request_at_a_time(dtype, tol):
         for x, y, z in zip(pa, pb, po):
             assert max(abs(u - v) for u, v in zip(x, y)) < tol
             assert max(abs(u - v) for u, v in zip(y, z)) < tol
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_lfm2_prefill_chunk_graphs_match_eager(dtype):
+    """The full-size prefill chunks replayed from CUDA graphs
+    (hybrid.ChunkGraphs) give the same readouts, bit for bit, as the eager
+    chunks: two prefixes (graphs captured on the first, replayed with new
+    ids, positions, arena rows and segment on the second), full chunks plus
+    an eager remainder, split-KV counts that change with the prefix length,
+    and a cached second pass over the first prefix (its tails copied out of
+    the static buffers)."""
+    from cev_b200 import hybrid
+    from cev_b200.engine import Request
+    cfg = configs.tiny_lfm2()
+    w = weights.init_weights(cfg, 43)
+    codes = workloads.code_ids(3)
+    outs = []
+    for graphs in (False, True):
+        dec = hybrid.Lfm2(cfg, w, dtype, "cuda", arena_rows=8192)
+        eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=64, pass_tokens=256,
+                                  prefix_cache_tokens=4096, chunk_graphs=graphs)
+        got = []
+        for seed, plen in ((9, 700), (10, 530), (9, 700)):
+            prefix, qs = workloads.decision_request(seed, plen, 4, 14, 28, 3, cfg["vocab_size"])
+            sfx = [q.render(codes, workloads.SEP_ID) for q in qs]
+            out = eng.run(Request(prefix, sfx, [3] * len(sfx)))
+            got.append(torch.stack([r.logits.float().cpu() for r in out.readouts]))
+        assert out.prefix_cached  # the third request reuses the first prefix's state
+        if graphs:
+            assert len(eng.graphs.graphs) >= 2
+        outs.append(got)
+    for a, b in zip(*outs):
+        assert torch.equal(a, b), (a - b).abs().max().item()

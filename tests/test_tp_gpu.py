@@ -1,6 +1,7 @@
 """The LFM2 attention layers split by KV-head group over 2 GPUs (NCCL
-all-gather of head outputs) against the unsplit model on one GPU: same
-request, f32, readouts within 1e-4.  Needs 2 GPUs (skipped otherwise)."""
+all-gather of head outputs), with the token-local layers on every token or
+split by token rows, against the unsplit model on one GPU: same request,
+f32, readouts within 1e-4.  Needs 2 GPUs (skipped otherwise)."""
 import os
 import socket
 
@@ -45,12 +46,15 @@ def _rank(rank, world, port, q):
         cfg = configs.tiny_lfm2()
         w = weights.init_weights(cfg, 41)
         D = cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"]
-        sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
-        split = _run(hybrid.Lfm2(cfg, w, torch.float32, f"cuda:{rank}", arena_rows=4096, split=sp), cfg)
+        outs = []
+        for token_split in (True, False):
+            sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
+            sp.sequence_parallel = token_split
+            outs.append(_run(hybrid.Lfm2(cfg, w, torch.float32, f"cuda:{rank}", arena_rows=4096, split=sp), cfg))
         err = None
         if rank == 0:
             whole = _run(hybrid.Lfm2(cfg, w, torch.float32, "cuda:0", arena_rows=4096), cfg)
-            err = (split - whole).abs().max().item()
+            err = max((o - whole).abs().max().item() for o in outs)
         dist.barrier()
         q.put((rank, err))
     finally:
