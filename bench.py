@@ -480,8 +480,11 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
                             cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"], rank, world)
         if os.environ.get("CEV_HEAD_GATHER", "fused") == "fused":
             # head outputs gathered by the attention epilogue over NVLink
-            # (largest call: 64 right-padded rows x 64 tokens)
-            split.enable_fused_gather(8192, dev)
+            # (largest call: 64 right-padded rows x 64 tokens); the token-local
+            # layers split by token rows, the residual stream gathered over
+            # NVLink peer stores
+            split.enable_fused_gather(8192, dev, hidden=cfg["hidden_size"])
+            split.sequence_parallel = True
     w = weights.init_weights(cfg, seed, torch.bfloat16, dev)
     if name == "cfg4":
         dec = hybrid.Qwen35(cfg, w, torch.bfloat16, dev, max_len=plen + 1024, arena_rows=plen + 8192)
@@ -490,9 +493,10 @@ def hybrid_decisions_bench(name: str, n_req: int, dev, world: int, dist_mod):
     del w
     codes = workloads.code_ids(4)
     # cfg4's state is run once: one 16384-token pass; cfg5's is prefilled in 512-token chunks
-    # cfg5's 128 state chunks on one GPU replay from CUDA graphs
+    # cfg5's 128 state chunks replay from CUDA graphs
+    graphs = name == "cfg5" and (split is None or split.fused is not None)
     eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=plen if name == "cfg4" else 512, pass_tokens=8192,
-                              prefix_cache_tokens=plen, chunk_graphs=name == "cfg5" and split is None)
+                              prefix_cache_tokens=plen, chunk_graphs=graphs)
     vocab = cfg["vocab_size"] - 1
     stream = 0 if split is not None else rank  # a split model runs the same requests on every rank
     reqs = [workloads.decision_request(20_000 * (stream + 1) + i, plen, nq, lo, hi, 4, vocab) for i in range(n_req + 1)]

@@ -177,6 +177,19 @@ int cevk_attn_packed_prefill_gather(const void* q, const void* k, const void* v,
                                     int32_t n_split, void* workspace, int64_t workspace_bytes, void* stream);
 int cevk_gather_signal(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch, void* stream);
 int cevk_gather_wait(const int32_t* flags, int32_t world, int32_t epoch, int64_t limit_cycles, void* stream);
+/* The same pair with the epoch in device memory (an int32 counter per rank,
+ * zeroed with the flags): the signal advances it and publishes the new
+ * value, the wait reads it -- so a CUDA graph can replay the calls, each
+ * replay a new epoch.  A process uses one form or the other. */
+int cevk_gather_signal_dev(int32_t* const* flags, int32_t world, int32_t rank, int32_t* epoch, void* stream);
+int cevk_gather_wait_dev(const int32_t* flags, int32_t world, const int32_t* epoch, int64_t limit_cycles,
+                         void* stream);
+/* `bytes` (a multiple of 16) from src to each of dst[0 .. n_dst) (this
+ * rank's and its peers' IPC buffers; 16-byte aligned): the residual
+ * stream's all-gather under the token split of the KV-head-split layers,
+ * followed by cevk_gather_signal_dev / cevk_gather_wait_dev.  No reference
+ * counterpart (the reference runs one process). */
+int cevk_rows_to_peers(const void* src, void* const* dst, int32_t n_dst, int64_t bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * Per-head RMSNorm + (partial) RoPE at explicit positions, writing Q and

@@ -44,6 +44,9 @@ SIGNATURES = {
                                                   F, I32, P, I64, P]),
     "cevk_gather_signal": (C.c_int, [P, I32, I32, I32, P]),
     "cevk_gather_wait": (C.c_int, [P, I32, I32, I64, P]),
+    "cevk_gather_signal_dev": (C.c_int, [P, I32, I32, P, P]),
+    "cevk_gather_wait_dev": (C.c_int, [P, I32, P, I64, P]),
+    "cevk_rows_to_peers": (C.c_int, [P, P, I32, I64, P]),
     "cevk_attn_split_workspace_size": (I64, [I32, I32, I32, I32]),
     "cevk_attn_packed_prefill_split": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32,
                                                  P, I64, I32, P]),

@@ -35,9 +35,6 @@ class HybridState:
     next_pos: int = 0
     gdn: dict = field(default_factory=dict)    # layer -> (conv tail [1,C,K-1], S [1,nv,dk,dv] f32)
     conv: dict = field(default_factory=dict)   # layer -> tail [1,d,K-1]
-    # token split over ranks: the rank whose conv tails are current (it ran
-    # the sequence's last token), or -1 when every rank's are
-    tail_rank: int = -1
     pins: int = 0
     released: bool = False
 
@@ -110,8 +107,6 @@ class _HybridDecoder:
             if self._token_split(B, T):
                 x = self._layers_token_split(ids, B, T, pos_t, rows_t, plan, state, keep)
             else:
-                if self.split is not None and state is not None and state.tail_rank >= 0:
-                    self._share_tails(state)
                 x = ops.embed(self.embed_w, ids)
                 h = ops.rms_norm(x, self.layers[0]["ln1"], self.eps, self.plus_one)
                 m = None
@@ -144,65 +139,56 @@ class _HybridDecoder:
             return False
         return B > 1 or T >= sp.world * max(getattr(self, "K", 1) - 1, 1)
 
-    def _share_tails(self, state):
-        """Every rank takes the short-conv tails of the rank that ran the
-        sequence's last token (one broadcast per conv layer, in layer order
-        on every rank)."""
-        for i, L in enumerate(self.layers):
-            if L["kind"] != "conv":
-                continue
-            t = state.conv.get(i)
-            if t is None:
-                t = state.conv[i] = torch.zeros(1, self.hidden, self.K - 1, dtype=self.dtype, device=self.device)
-            self.split.broadcast(t, state.tail_rank)
-        state.tail_rank = -1
+    def _token_runs(self, B, T):
+        """This rank's token rows [a, b) of the token split, and the run
+        length (all but the last runs are full)."""
+        sp = self.split
+        if B > 1:
+            per = -(-B // sp.world)
+            return min(B, sp.rank * per) * T, min(B, (sp.rank + 1) * per) * T, per * T
+        unit = -(-T // sp.world)
+        return min(T, sp.rank * unit), min(T, (sp.rank + 1) * unit), unit
 
-    def _layers_token_split(self, ids, B, T, pos_t, rows_t, plan, state, keep):
+    def _layers_token_split(self, ids, B, T, pos_t, rows_t, plan, state, keep, tails=None):
         """The layer loop with a KV-head split over ranks: attention runs
         this rank's heads on every token (its head outputs gathered across
         ranks), everything token-local -- the output projection, the short
         conv, the MLP, the norms -- runs only on this rank's token rows, and
-        one all-gather per layer rebuilds the residual stream on every rank.
-        A row batch splits by whole rows (each continues the state's conv
-        tails, shared first).  A sequence chunk splits into contiguous runs,
-        the first run on the rank holding the conv tails; a later run's
-        short conv also runs over the K-1 tokens before it (their outputs
-        are dropped), and the rank that runs the chunk's last token keeps
-        the new tails."""
+        one all-gather per layer rebuilds the residual stream on every rank
+        (NVLink peer stores into the fused gather's row buffers, or NCCL).
+        A row batch splits by whole rows, a sequence chunk into contiguous
+        runs in rank order; a later run's short conv also runs over the K-1
+        tokens before it (their outputs are dropped), and with ``keep``
+        every rank recomputes the sequence's new conv tails from the
+        gathered stream, so every rank's state stays whole.  ``tails``:
+        (read, write) tail buffers by layer for a graph-captured chunk."""
         sp = self.split
         n = B * T
-        if B > 1:
-            if state is not None and state.tail_rank >= 0:
-                self._share_tails(state)
-            per = -(-B // sp.world)
-            a, b, unit = min(B, sp.rank * per) * T, min(B, (sp.rank + 1) * per) * T, per * T
-            runs = None
+        a, b, unit = self._token_runs(B, T)
+        fused = sp.fused if sp.fused is not None and sp.fused.hidden == self.hidden else None
+        if fused is not None:
+            k = 0
+            x = ops.embed(self.embed_w, ids, out=fused.rows[0][:n])
         else:
-            unit = -(-T // sp.world)
-            first = 0 if state is None or state.tail_rank < 0 else state.tail_rank
-            runs = [(r - first) % sp.world for r in range(sp.world)]  # run index of each rank
-            a, b = min(T, runs[sp.rank] * unit), min(T, (runs[sp.rank] + 1) * unit)
-        x = ops.embed(self.embed_w, ids)
+            x = ops.embed(self.embed_w, ids)
         for i, L in enumerate(self.layers):
             if L["kind"] == "attn":
                 h = ops.rms_norm(x, L["ln1"], self.eps, self.plus_one)
                 ctx = self._attn_ctx(i, L, h, pos_t, rows_t, plan)
                 o = F.linear(ctx[a:b], L["o"]) if b > a else None
             elif L["kind"] == "conv":
-                o = self._conv_rows(i, L, x, a, b, B, T, state, keep)
+                o = self._conv_rows(i, L, x, a, b, B, T, state, keep, tails)
             else:
                 raise NotImplementedError("token split: attention and short-conv layers only")
             if b > a:
                 xs = x[a:b]
                 hs = ops.add_rms_norm(xs, o, L["ln2"], self.eps, self.plus_one)
                 ops.residual_add(xs, F.linear(ops.swiglu(F.linear(hs, L["gu"])), L["down"]))
-            if runs is None:
-                sp.gather_rows(x, a, b, unit)
+            if fused is not None:
+                x = fused.gather_rows(k, a, b, n)
+                k = 1 - k
             else:
-                sp.gather_runs(x, a, b, unit, runs)
-        if keep and runs is not None:
-            last = (T - 1) // unit
-            state.tail_rank = runs.index(last)
+                sp.gather_rows(x, a, b, unit)
         return x
 
     def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot, attend=None):
@@ -355,35 +341,46 @@ class Lfm2(_HybridDecoder):
             state.conv[i] = tail_out
         return F.linear(y, L["out"])
 
-    def _conv_rows(self, i, L, x, a, b, B, T, state, keep):
+    def _conv_rows(self, i, L, x, a, b, B, T, state, keep, tails=None):
         """ShortConv::forward (lfm2.rs:199-219) on token rows [a, b) of the
         residual stream x [B*T, H]: whole rows continuing the state's tails
         (B > 1), or a run of one sequence, computed over the K-1 tokens
-        before it too (its first K-1 outputs are dropped) unless it starts
-        the sequence, where the state's tails precede it.  The run holding
-        the sequence's last token writes the new tails."""
+        before it too (their outputs are dropped) unless it starts the
+        sequence, where the state's tails precede it.  With ``keep`` every
+        rank derives the sequence's new tails (B * x of the in_proj output
+        of its last K-1 tokens, rounded to the model dtype as the conv
+        kernel rounds its inputs) from the same stream rows."""
         d, K = self.hidden, self.K
-        tail_prev = None if state is None else state.conv.get(i)
-        if b <= a:
-            return None
-        if B > 1:
-            bcx = F.linear(ops.rms_norm(x[a:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
-            y = ops.short_conv(bcx, (b - a) // T, T, d, L["conv_w"], L["bias"], tail_prev, None)
-            return F.linear(y, L["out"])
-        lo = max(0, a - (K - 1))
-        tail_out = None
-        if keep and b == T:
-            tail_out = torch.empty(1, d, K - 1, dtype=self.dtype, device=self.device)
-        bcx = F.linear(ops.rms_norm(x[lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
-        y = ops.short_conv(bcx, 1, b - lo, d, L["conv_w"], L["bias"], tail_prev if a == 0 else None, tail_out)
-        if tail_out is not None:
-            state.conv[i] = tail_out
-        return F.linear(y[a - lo:], L["out"])
+        tail_prev = tails[0][i] if tails is not None else (None if state is None else state.conv.get(i))
+        out = None
+        if b > a:
+            if B > 1:
+                bcx = F.linear(ops.rms_norm(x[a:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+                y = ops.short_conv(bcx, (b - a) // T, T, d, L["conv_w"], L["bias"], tail_prev, None)
+                out = F.linear(y, L["out"])
+            else:
+                lo = max(0, a - (K - 1))
+                bcx = F.linear(ops.rms_norm(x[lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+                y = ops.short_conv(bcx, 1, b - lo, d, L["conv_w"], L["bias"], tail_prev if a == 0 else None, None)
+                out = F.linear(y[a - lo:], L["out"])
+        if keep:
+            lo = max(0, T - (K - 1))
+            hb = F.linear(ops.rms_norm(x[lo:T], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+            cur = (hb[:, :d] * hb[:, 2 * d:]).t()
+            if T - lo < K - 1:  # a chunk shorter than the tail keeps part of the previous one
+                prev = tail_prev[0] if tail_prev is not None else torch.zeros(d, K - 1, dtype=x.dtype, device=x.device)
+                cur = torch.cat([prev[:, T - lo:], cur], 1)
+            if tails is not None:
+                tails[1][i][0].copy_(cur)
+            else:
+                state.conv[i] = cur.unsqueeze(0).contiguous()
+        return out
 
 
 class ChunkGraphs:
     """The full-size prefill chunks of an LFM2 decoder (short-conv and
-    attention layers, one GPU) replayed from CUDA graphs.
+    attention layers; one GPU, or a KV-head split whose gathers run over
+    NVLink peer memory with device-side epochs) replayed from CUDA graphs.
 
     A 512-token chunk of the cfg5 state is ~150 kernel launches whose host
     cost (Python, torch dispatch, ctypes) rivals their device time; a graph
@@ -400,8 +397,10 @@ class ChunkGraphs:
 
     def __init__(self, dec: "Lfm2", T: int):
         from ._lib import Segment
-        if dec.split is not None or any(L["kind"] not in ("conv", "attn") for L in dec.layers):
-            raise ValueError("chunk graphs: one-GPU LFM2 decoders only")
+        if any(L["kind"] not in ("conv", "attn") for L in dec.layers):
+            raise ValueError("chunk graphs: LFM2 decoders only")
+        if dec.split is not None and dec.split.fused is None:
+            raise ValueError("chunk graphs: a KV-head split needs the fused (peer-memory) gathers")
         self.dec, self.T = dec, T
         dev = dec.device
         # pinned staging ring: a slot is rewritten only after its copy ran
@@ -439,6 +438,8 @@ class ChunkGraphs:
     def _body(self, plan, parity: int):
         dec, T = self.dec, self.T
         rd, wr = self.tails[parity], self.tails[1 - parity]
+        if dec._token_split(1, T):
+            return dec._layers_token_split(self.ids, 1, T, self.pos, self.rows, plan, None, True, tails=(rd, wr))
         x = ops.embed(dec.embed_w, self.ids)
         h = ops.rms_norm(x, dec.layers[0]["ln1"], dec.eps, dec.plus_one)
         m = None
@@ -519,8 +520,8 @@ class HybridEngine:
 
     def __init__(self, decoder: _HybridDecoder, code_ids, pad_id: int, prefill_chunk=512, pass_tokens=2048,
                  prefix_cache_tokens=65536, device_readout=False, chunk_graphs=False):
-        """``chunk_graphs``: replay the full-size prefill chunks of a
-        one-GPU LFM2 decoder from CUDA graphs (:class:`ChunkGraphs`)."""
+        """``chunk_graphs``: replay the full-size prefill chunks of an LFM2
+        decoder from CUDA graphs (:class:`ChunkGraphs`)."""
         self.device_readout = device_readout  # readouts stay on the device (on-device debias)
         self.decoder = decoder
         self.graphs = ChunkGraphs(decoder, prefill_chunk) if chunk_graphs else None

@@ -31,12 +31,13 @@ class KvHeadSplit:
         # stream all-gathered after each layer (False: every rank runs them
         # on every token)
         self.sequence_parallel = False
-        self._run_index = {}
 
-    def enable_fused_gather(self, max_tokens: int, device) -> "FusedHeadGather":
+    def enable_fused_gather(self, max_tokens: int, device, hidden: int = 0) -> "FusedHeadGather":
         """Gather head outputs from the attention epilogue over NVLink peer
-        memory instead of the NCCL all-gather (bf16 models)."""
-        self.fused = FusedHeadGather(self, max_tokens, device, self.group)
+        memory instead of the NCCL all-gather (bf16 models); with ``hidden``
+        also the residual stream of the token split (``max_tokens`` rows of
+        that width) over peer stores instead of NCCL."""
+        self.fused = FusedHeadGather(self, max_tokens, device, self.group, hidden=hidden)
         return self.fused
 
     def slice_fused_qkv(self, w: torch.Tensor) -> torch.Tensor:
@@ -63,35 +64,6 @@ class KvHeadSplit:
         out = x.new_empty(self.world * unit, H)
         dist.all_gather_into_tensor(out, send, group=self.group)
         x.copy_(out[:n])
-
-    def gather_runs(self, x: torch.Tensor, a: int, b: int, unit: int, runs) -> None:
-        """Like :meth:`gather_rows` for a sequence whose runs are assigned
-        by rotation: rank r holds run ``runs[r]`` (rows [runs[r] * unit,
-        ...)), this rank's being [a, b)."""
-        if all(runs[r] == r for r in range(self.world)):
-            self.gather_rows(x, a, b, unit)
-            return
-        n, H = x.shape
-        flat = x.new_empty(self.world * unit, H)
-        if b - a == unit:
-            dist.all_gather_into_tensor(flat, x[a:b], group=self.group)
-        else:
-            send = x.new_zeros(unit, H)
-            send[:b - a] = x[a:b]
-            dist.all_gather_into_tensor(flat, send, group=self.group)
-        out = flat.view(self.world, unit, H)
-        if n == self.world * unit:
-            key = (tuple(runs), x.device)
-            idx = self._run_index.get(key)
-            if idx is None:
-                idx = self._run_index[key] = torch.tensor(runs, device=x.device)
-            x.view(self.world, unit, H).index_copy_(0, idx, out)
-            return
-        for r in range(self.world):
-            lo = runs[r] * unit
-            hi = min(n, lo + unit)
-            if hi > lo and r != self.rank:
-                x[lo:hi] = out[r, :hi - lo]
 
     def broadcast(self, t: torch.Tensor, src: int) -> None:
         """t from rank ``src`` to every rank, in place."""
@@ -125,7 +97,8 @@ class FusedHeadGather:
     then reads the local buffer.  Two buffers alternate by epoch parity.
     Every rank must make the same sequence of ``attend`` calls."""
 
-    def __init__(self, split: KvHeadSplit, max_tokens: int, device, group=None, limit_cycles: int = 1 << 31):
+    def __init__(self, split: KvHeadSplit, max_tokens: int, device, group=None, limit_cycles: int = 1 << 31,
+                 hidden: int = 0):
         import ctypes as C
 
         from ._lib import check, lib
@@ -133,9 +106,16 @@ class FusedHeadGather:
         self.width = split.hq * split.D
         self.max_tokens = max_tokens
         self.buf_bytes = max_tokens * self.width * 2
-        self.flag_off = 2 * self.buf_bytes
+        # residual-stream rows of the token split: two buffers (layer parity)
+        self.hidden = hidden
+        self.row_bytes = max_tokens * hidden * 2
+        self.row_off = 2 * self.buf_bytes
+        # flags [world] int32, then this rank's epoch counter (device side:
+        # the signal kernel advances it, so graph replays get new epochs)
+        self.flag_off = self.row_off + 2 * self.row_bytes
+        self.ctr_off = self.flag_off + 128
         self.limit = limit_cycles
-        self.epoch = 0
+        self.epoch = 0  # host count of gathers: picks the head buffer by parity
         self.device = torch.device(device)
         ptr = C.c_void_p()
         check(lib().cevk_ipc_alloc(self.flag_off + 256, C.byref(ptr)))
@@ -156,7 +136,37 @@ class FusedHeadGather:
         self.flag_ptrs = (C.c_void_p * self.world)(*[b + self.flag_off for b in self.bases])
         self.views = [torch.as_tensor(_DeviceView(self.own + k * self.buf_bytes, (max_tokens, self.width)),
                                       device=self.device).view(torch.bfloat16) for k in (0, 1)]
+        self.rows = [torch.as_tensor(_DeviceView(self.own + self.row_off + k * self.row_bytes, (max_tokens, hidden)),
+                                     device=self.device).view(torch.bfloat16) for k in (0, 1)] if hidden else []
+        self.ctr = C.c_void_p(self.own + self.ctr_off)
         self.group = group
+
+    def _signal_wait(self, s) -> None:
+        import ctypes as C
+
+        from ._lib import check, lib
+        self.epoch += 1
+        check(lib().cevk_gather_signal_dev(self.flag_ptrs, self.world, self.rank, self.ctr, s))
+        check(lib().cevk_gather_wait_dev(C.c_void_p(self.own + self.flag_off), self.world, self.ctr, self.limit, s))
+
+    def gather_rows(self, k: int, a: int, b: int, n: int) -> torch.Tensor:
+        """Rows [a, b) of this rank's residual buffer k stored into every
+        rank's buffer 1 - k over NVLink, then the epoch handshake: returns
+        this rank's buffer 1 - k, [n, hidden], complete.  (Buffers alternate
+        by layer: a peer writes layer l's rows into buffer 1 - k only after
+        every rank signalled layer l - 1, i.e. finished reading it.)"""
+        import ctypes as C
+
+        from . import ops
+        from ._lib import check, lib
+        rb = self.hidden * 2
+        if b > a:
+            dst = (C.c_void_p * self.world)(*[base + self.row_off + (1 - k) * self.row_bytes + a * rb
+                                              for base in self.bases])
+            src = C.c_void_p(self.own + self.row_off + k * self.row_bytes + a * rb)
+            check(lib().cevk_rows_to_peers(src, dst, self.world, (b - a) * rb, ops._s()))
+        self._signal_wait(ops._s())
+        return self.rows[1 - k][:n]
 
     def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan, scale=None) -> torch.Tensor:
         """This rank's heads of the packed attention (q [T, Hq/world, D],
@@ -174,8 +184,7 @@ class FusedHeadGather:
         if q.dtype != torch.bfloat16 or plan.n_tokens != T:
             raise ValueError("fused head gather: bf16 and a plan for these tokens")
         scale = 1.0 / math.sqrt(D) if scale is None else scale
-        self.epoch += 1
-        e = self.epoch
+        e = self.epoch + 1
         off = (e & 1) * self.buf_bytes + self.split.q0 * D * 2
         dst = (C.c_void_p * self.world)(*[b + off for b in self.bases])
         ws = plan.workspace
@@ -184,8 +193,7 @@ class FusedHeadGather:
             ops._p(q), ops._p(k), ops._p(v), dst, self.world, T, k.shape[0], hq, k.shape[1], D, q.stride(0),
             k.stride(0), self.width, ops._p(plan.dev), plan.n_segs, plan.n_tiles, scale, plan.n_split, ops._p(ws),
             0 if ws is None else ws.numel(), s))
-        check(lib().cevk_gather_signal(self.flag_ptrs, self.world, self.rank, e, s))
-        check(lib().cevk_gather_wait(C.c_void_p(self.own + self.flag_off), self.world, e, self.limit, s))
+        self._signal_wait(s)
         return self.views[e & 1][:T]
 
     def close(self) -> None:

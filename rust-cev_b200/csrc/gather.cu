@@ -10,6 +10,7 @@
 // until all flags of its own array reach the epoch before the replicated
 // output projection reads the buffer.  Replaces the NCCL all-gather of
 // lfm2.rs:145-171's per-head outputs under the KV-head split.
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -51,6 +52,59 @@ __global__ void gather_wait_kernel(const int* flags, int world, int epoch, long 
       }
       __nanosleep(64);
     }
+  }
+}
+
+// Device-side epochs: the signal kernel advances this rank's epoch counter
+// and publishes it; the wait kernel reads the same counter.  A CUDA graph
+// can then replay the same launches, each replay a new epoch.
+__global__ void gather_signal_dev_kernel(FlagPtrs flags, int world, int rank, int* epoch_ctr) {
+  __shared__ int e;
+  if (threadIdx.x == 0) {
+    e = *epoch_ctr + 1;
+    *epoch_ctr = e;
+  }
+  __syncthreads();
+  const int i = threadIdx.x;
+  if (i >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.p[i] + rank), "r"(e) : "memory");
+}
+
+__global__ void gather_wait_dev_kernel(const int* flags, int world, const int* epoch_ctr, long long limit) {
+  if (threadIdx.x != 0) return;
+  const int epoch = *epoch_ctr;  // this rank's signal kernel ran earlier on the stream
+  const long long t0 = clock64();
+  for (int s = 0; s < world; ++s) {
+    for (;;) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+      if (v - epoch >= 0) break;
+      if (clock64() - t0 > limit) {
+        if (atomicExch(&g_device_error, kErrGatherTimeout) == 0) {
+          g_device_error_info[0] = (int)blockIdx.x;
+          g_device_error_info[1] = s;
+          g_device_error_info[2] = v;
+          g_device_error_info[3] = epoch;
+        }
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+// One contiguous range of 16-byte words copied to each destination (this
+// rank's buffer and its peers', over NVLink); every word is loaded once.
+struct DstPtrs {
+  uint4* p[kMaxRanks];
+};
+__global__ void __launch_bounds__(256) rows_to_peers_kernel(const uint4* __restrict__ src, DstPtrs dst, int n_dst,
+                                                            long long n16) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 v = src[i];
+    for (int d = 0; d < n_dst; ++d) dst.p[d][i] = v;
   }
 }
 
@@ -117,6 +171,42 @@ int cevk_gather_wait(const int32_t* flags, int32_t world, int32_t epoch, int64_t
     return set_error(CEVK_E_SHAPE, "gather_wait: world %d epoch %d", world, epoch);
   gather_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, world, epoch, limit_cycles);
   return check_launch("gather_wait_kernel");
+}
+
+int cevk_gather_signal_dev(int32_t* const* flags, int32_t world, int32_t rank, int32_t* epoch, void* stream) {
+  if (!flags || !epoch || world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return set_error(CEVK_E_SHAPE, "gather_signal_dev: world %d rank %d", world, rank);
+  FlagPtrs f{};
+  for (int i = 0; i < world; ++i) {
+    if (!flags[i]) return set_error(CEVK_E_SHAPE, "gather_signal_dev: null flag array %d", i);
+    f.p[i] = flags[i];
+  }
+  gather_signal_dev_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(f, world, rank, epoch);
+  return check_launch("gather_signal_dev_kernel");
+}
+
+int cevk_gather_wait_dev(const int32_t* flags, int32_t world, const int32_t* epoch, int64_t limit_cycles,
+                         void* stream) {
+  if (!flags || !epoch || world < 1 || world > kMaxRanks || limit_cycles <= 0)
+    return set_error(CEVK_E_SHAPE, "gather_wait_dev: world %d", world);
+  gather_wait_dev_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, world, epoch, limit_cycles);
+  return check_launch("gather_wait_dev_kernel");
+}
+
+int cevk_rows_to_peers(const void* src, void* const* dst, int32_t n_dst, int64_t bytes, void* stream) {
+  if (!src || !dst || n_dst < 1 || n_dst > kMaxRanks || bytes < 0 || (bytes & 15) || ((uintptr_t)src & 15))
+    return set_error(CEVK_E_SHAPE, "rows_to_peers: %d destinations, %lld bytes", n_dst, (long long)bytes);
+  DstPtrs d{};
+  for (int i = 0; i < n_dst; ++i) {
+    if (!dst[i] || ((uintptr_t)dst[i] & 15)) return set_error(CEVK_E_SHAPE, "rows_to_peers: destination %d", i);
+    d.p[i] = reinterpret_cast<uint4*>(dst[i]);
+  }
+  const long long n16 = bytes / 16;
+  if (n16 == 0) return CEVK_OK;
+  const long long blocks = std::min<long long>((n16 + 255) / 256, 148 * 8);
+  rows_to_peers_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(src), d, n_dst, n16);
+  return check_launch("rows_to_peers_kernel");
 }
 
 }  // extern "C"

@@ -65,6 +65,12 @@ unsafe extern "C" {
                                            workspace: *mut c_void, workspace_bytes: i64, stream: *mut c_void) -> i32;
     pub fn cevk_gather_signal(flags: *const *mut i32, world: i32, rank: i32, epoch: i32, stream: *mut c_void) -> i32;
     pub fn cevk_gather_wait(flags: *const i32, world: i32, epoch: i32, limit_cycles: i64, stream: *mut c_void) -> i32;
+    pub fn cevk_gather_signal_dev(flags: *const *mut i32, world: i32, rank: i32, epoch: *mut i32, stream: *mut c_void)
+        -> i32;
+    pub fn cevk_gather_wait_dev(flags: *const i32, world: i32, epoch: *const i32, limit_cycles: i64,
+                                stream: *mut c_void) -> i32;
+    pub fn cevk_rows_to_peers(src: *const c_void, dst: *const *mut c_void, n_dst: i32, bytes: i64,
+                              stream: *mut c_void) -> i32;
     pub fn cevk_qk_norm_rope(qkv: *const c_void, row_stride: i32, q_head_stride: i32, k_col: i32, v_col: i32,
                              q_norm_w: *const c_void, k_norm_w: *const c_void, eps: f32, norm_plus_one: i32,
                              pos: *const i32, theta: f64, rotary_dim: i32, q_out: *mut c_void,

@@ -24,11 +24,11 @@ def _request(cfg):
     return codes, prefix, [q.render(codes, workloads.SEP_ID) for q in qs]
 
 
-def _run(model, cfg):
+def _run(model, cfg, graphs=False):
     from cev_b200 import hybrid
     from cev_b200.engine import Request
     codes, prefix, sfx = _request(cfg)
-    eng = hybrid.HybridEngine(model, codes, pad_id=0, prefill_chunk=128, pass_tokens=256)
+    eng = hybrid.HybridEngine(model, codes, pad_id=0, prefill_chunk=128, pass_tokens=256, chunk_graphs=graphs)
     out = eng.run(Request(prefix, sfx, [3] * len(sfx)))
     return torch.stack([r.logits.float().cpu() for r in out.readouts])
 
@@ -80,7 +80,9 @@ def test_lfm2_kv_head_split_matches_unsplit():
 def _rank_fused(rank, world, port, q):
     """bf16: the split engine with the fused head gather (attention epilogue
     stores into every rank's buffer over NVLink) against the same split
-    engine with the NCCL all-gather: same kernels, same bits."""
+    engine with the NCCL all-gather: same kernels, same bits.  Likewise with
+    the token split (residual stream over NVLink peer stores vs NCCL), and
+    its prefill chunks replayed from CUDA graphs (device-side epochs)."""
     import torch.distributed as dist
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -88,25 +90,32 @@ def _rank_fused(rank, world, port, q):
     from datetime import timedelta
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
                             timeout=timedelta(seconds=60))
-    fused = None
+    gathers = []
     try:
-        from cev_b200 import configs, hybrid, weights
+        from cev_b200 import configs, hybrid, ops, weights
         from cev_b200.tp import KvHeadSplit
         cfg = configs.tiny_lfm2()
         w = weights.init_weights(cfg, 42)
         D = cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"]
         dev = f"cuda:{rank}"
-        sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
-        nccl = _run(hybrid.Lfm2(cfg, w, torch.bfloat16, dev, arena_rows=4096, split=sp), cfg)
-        sp2 = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
-        fused = sp2.enable_fused_gather(1024, dev)
-        got = _run(hybrid.Lfm2(cfg, w, torch.bfloat16, dev, arena_rows=4096, split=sp2), cfg)
-        from cev_b200 import ops
-        ops.device_status()
-        q.put((rank, (got - nccl).abs().max().item(), fused.epoch))
+
+        def run(fused, token_split, graphs=False):
+            sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
+            sp.sequence_parallel = token_split
+            if fused:
+                gathers.append(sp.enable_fused_gather(1024, dev, hidden=cfg["hidden_size"] if token_split else 0))
+            out = _run(hybrid.Lfm2(cfg, w, torch.bfloat16, dev, arena_rows=4096, split=sp), cfg, graphs)
+            ops.device_status()
+            return out
+
+        nccl, got = run(False, False), run(True, False)
+        nccl_ts, fused_ts, graph_ts = run(False, True), run(True, True), run(True, True, graphs=True)
+        q.put((rank, (got - nccl).abs().max().item(), (fused_ts - nccl_ts).abs().max().item(),
+               (graph_ts - fused_ts).abs().max().item(), (nccl_ts - nccl).abs().max().item(),
+               min(g.epoch for g in gathers)))
     finally:
-        if fused is not None:
-            fused.close()
+        for g in gathers:
+            g.close()
         dist.destroy_process_group()
 
 
@@ -122,7 +131,8 @@ def test_lfm2_fused_head_gather_matches_nccl_gather():
     for p in procs:
         p.join(300)
         assert p.exitcode == 0
-    res = {r: (err, ep) for r, err, ep in (q.get(timeout=10) for _ in range(2))}
+    res = {v[0]: v[1:] for v in (q.get(timeout=10) for _ in range(2))}
     for r in (0, 1):
-        err, epochs = res[r]
-        assert epochs > 0 and err == 0.0, res
+        err, err_ts, err_graph, err_split, epochs = res[r]
+        assert epochs > 0 and err == 0.0 and err_ts == 0.0 and err_graph == 0.0, res
+        assert err_split < 0.1, res  # token split vs not: same math, other GEMM shapes (bf16)
