@@ -190,6 +190,16 @@ int cevk_gather_wait_dev(const int32_t* flags, int32_t world, const int32_t* epo
  * followed by cevk_gather_signal_dev / cevk_gather_wait_dev.  No reference
  * counterpart (the reference runs one process). */
 int cevk_rows_to_peers(const void* src, void* const* dst, int32_t n_dst, int64_t bytes, void* stream);
+/* cevk_gather_signal_dev + cevk_gather_wait_dev in one launch. */
+int cevk_gather_sync_dev(int32_t* const* flags, int32_t world, int32_t rank, int32_t* epoch, const int32_t* own_flags,
+                         int64_t limit_cycles, void* stream);
+/* cevk_rows_to_peers + cevk_gather_sync_dev in one launch (the last block
+ * to finish its copies signals and waits).  `ticket`: a device uint32,
+ * zero-initialised, that the launch leaves at zero; one per stream of
+ * calls. */
+int cevk_rows_gather_dev(const void* src, void* const* dst, int32_t n_dst, int64_t bytes, int32_t* const* flags,
+                         int32_t world, int32_t rank, int32_t* epoch, const int32_t* own_flags, int64_t limit_cycles,
+                         uint32_t* ticket, void* stream);
 
 /* ------------------------------------------------------------------------
  * Per-head RMSNorm + (partial) RoPE at explicit positions, writing Q and

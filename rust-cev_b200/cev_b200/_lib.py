@@ -47,6 +47,8 @@ SIGNATURES = {
     "cevk_gather_signal_dev": (C.c_int, [P, I32, I32, P, P]),
     "cevk_gather_wait_dev": (C.c_int, [P, I32, P, I64, P]),
     "cevk_rows_to_peers": (C.c_int, [P, P, I32, I64, P]),
+    "cevk_gather_sync_dev": (C.c_int, [P, I32, I32, P, P, I64, P]),
+    "cevk_rows_gather_dev": (C.c_int, [P, P, I32, I64, P, I32, I32, P, P, I64, P, P]),
     "cevk_attn_split_workspace_size": (I64, [I32, I32, I32, I32]),
     "cevk_attn_packed_prefill_split": (C.c_int, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, P, I32, I32, F, I32,
                                                  P, I64, I32, P]),

@@ -165,19 +165,30 @@ class _HybridDecoder:
         sp = self.split
         n = B * T
         a, b, unit = self._token_runs(B, T)
+        K1 = getattr(self, "K", 1) - 1
         fused = sp.fused if sp.fused is not None and sp.fused.hidden == self.hidden else None
+        if fused is not None and n + K1 > fused.max_tokens:
+            raise ValueError(f"{n} tokens: the residual buffers hold {fused.max_tokens - K1}")
         if fused is not None:
             k = 0
             x = ops.embed(self.embed_w, ids, out=fused.rows[0][:n])
         else:
             x = ops.embed(self.embed_w, ids)
+        # With the peer-store gather, the rank that runs a sequence's last
+        # token writes each conv layer's new tails (d x (K-1) values) into
+        # the K-1 rows after the stream and sends them with its rows.
+        ships_tails = fused is not None and keep and b == T and b > a
         for i, L in enumerate(self.layers):
+            conv_tail = L["kind"] == "conv" and keep and fused is not None
             if L["kind"] == "attn":
                 h = ops.rms_norm(x, L["ln1"], self.eps, self.plus_one)
                 ctx = self._attn_ctx(i, L, h, pos_t, rows_t, plan)
                 o = F.linear(ctx[a:b], L["o"]) if b > a else None
             elif L["kind"] == "conv":
-                o = self._conv_rows(i, L, x, a, b, B, T, state, keep, tails)
+                dst = None
+                if conv_tail and ships_tails:
+                    dst = fused.rows[k][n:n + K1].reshape(-1)[:self.hidden * K1].view(1, self.hidden, K1)
+                o = self._conv_rows(i, L, x, a, b, B, T, state, keep and not conv_tail, tails, tail_dst=dst)
             else:
                 raise NotImplementedError("token split: attention and short-conv layers only")
             if b > a:
@@ -185,8 +196,14 @@ class _HybridDecoder:
                 hs = ops.add_rms_norm(xs, o, L["ln2"], self.eps, self.plus_one)
                 ops.residual_add(xs, F.linear(ops.swiglu(F.linear(hs, L["gu"])), L["down"]))
             if fused is not None:
-                x = fused.gather_rows(k, a, b, n)
+                x = fused.gather_rows(k, a, b + (K1 if conv_tail and ships_tails else 0), n)
                 k = 1 - k
+                if conv_tail:
+                    got = fused.rows[k][n:n + K1].reshape(-1)[:self.hidden * K1].view(1, self.hidden, K1)
+                    if tails is not None:
+                        tails[1][i].copy_(got)
+                    else:
+                        state.conv[i] = got.clone()
             else:
                 sp.gather_rows(x, a, b, unit)
         return x
@@ -341,7 +358,7 @@ class Lfm2(_HybridDecoder):
             state.conv[i] = tail_out
         return F.linear(y, L["out"])
 
-    def _conv_rows(self, i, L, x, a, b, B, T, state, keep, tails=None):
+    def _conv_rows(self, i, L, x, a, b, B, T, state, keep, tails=None, tail_dst=None):
         """ShortConv::forward (lfm2.rs:199-219) on token rows [a, b) of the
         residual stream x [B*T, H]: whole rows continuing the state's tails
         (B > 1), or a run of one sequence, computed over the K-1 tokens
@@ -349,7 +366,9 @@ class Lfm2(_HybridDecoder):
         sequence, where the state's tails precede it.  With ``keep`` every
         rank derives the sequence's new tails (B * x of the in_proj output
         of its last K-1 tokens, rounded to the model dtype as the conv
-        kernel rounds its inputs) from the same stream rows."""
+        kernel rounds its inputs) from the same stream rows; ``tail_dst``
+        instead takes the tails the conv kernel writes for the run that
+        ends the sequence (the peer-store gather ships them)."""
         d, K = self.hidden, self.K
         tail_prev = tails[0][i] if tails is not None else (None if state is None else state.conv.get(i))
         out = None
@@ -361,7 +380,8 @@ class Lfm2(_HybridDecoder):
             else:
                 lo = max(0, a - (K - 1))
                 bcx = F.linear(ops.rms_norm(x[lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
-                y = ops.short_conv(bcx, 1, b - lo, d, L["conv_w"], L["bias"], tail_prev if a == 0 else None, None)
+                y = ops.short_conv(bcx, 1, b - lo, d, L["conv_w"], L["bias"], tail_prev if a == 0 else None,
+                                   tail_dst)
                 out = F.linear(y[a - lo:], L["out"])
         if keep:
             lo = max(0, T - (K - 1))

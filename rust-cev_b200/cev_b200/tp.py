@@ -139,15 +139,15 @@ class FusedHeadGather:
         self.rows = [torch.as_tensor(_DeviceView(self.own + self.row_off + k * self.row_bytes, (max_tokens, hidden)),
                                      device=self.device).view(torch.bfloat16) for k in (0, 1)] if hidden else []
         self.ctr = C.c_void_p(self.own + self.ctr_off)
+        self.ticket = C.c_void_p(self.own + self.ctr_off + 64)  # the row gather's last-block ticket
+        self.own_flags = C.c_void_p(self.own + self.flag_off)
         self.group = group
 
     def _signal_wait(self, s) -> None:
-        import ctypes as C
-
         from ._lib import check, lib
         self.epoch += 1
-        check(lib().cevk_gather_signal_dev(self.flag_ptrs, self.world, self.rank, self.ctr, s))
-        check(lib().cevk_gather_wait_dev(C.c_void_p(self.own + self.flag_off), self.world, self.ctr, self.limit, s))
+        check(lib().cevk_gather_sync_dev(self.flag_ptrs, self.world, self.rank, self.ctr, self.own_flags, self.limit,
+                                         s))
 
     def gather_rows(self, k: int, a: int, b: int, n: int) -> torch.Tensor:
         """Rows [a, b) of this rank's residual buffer k stored into every
@@ -160,12 +160,13 @@ class FusedHeadGather:
         from . import ops
         from ._lib import check, lib
         rb = self.hidden * 2
-        if b > a:
-            dst = (C.c_void_p * self.world)(*[base + self.row_off + (1 - k) * self.row_bytes + a * rb
-                                              for base in self.bases])
-            src = C.c_void_p(self.own + self.row_off + k * self.row_bytes + a * rb)
-            check(lib().cevk_rows_to_peers(src, dst, self.world, (b - a) * rb, ops._s()))
-        self._signal_wait(ops._s())
+        a = min(a, b)
+        dst = (C.c_void_p * self.world)(*[base + self.row_off + (1 - k) * self.row_bytes + a * rb
+                                          for base in self.bases])
+        src = C.c_void_p(self.own + self.row_off + k * self.row_bytes + a * rb)
+        self.epoch += 1
+        check(lib().cevk_rows_gather_dev(src, dst, self.world, (b - a) * rb, self.flag_ptrs, self.world, self.rank,
+                                         self.ctr, self.own_flags, self.limit, self.ticket, ops._s()))
         return self.rows[1 - k][:n]
 
     def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan, scale=None) -> torch.Tensor:

@@ -108,6 +108,71 @@ __global__ void __launch_bounds__(256) rows_to_peers_kernel(const uint4* __restr
   }
 }
 
+// Signal and wait in one launch (device-side epoch): the head gather's
+// handshake after the attention call.
+__device__ __forceinline__ void signal_then_wait(const FlagPtrs& flags, int world, int rank, int* epoch_ctr,
+                                                 const int* own, long long limit) {
+  __shared__ int e;
+  if (threadIdx.x == 0) {
+    e = *epoch_ctr + 1;
+    *epoch_ctr = e;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < world) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.p[threadIdx.x] + rank), "r"(e) : "memory");
+  }
+  if (threadIdx.x != 0) return;
+  const long long t0 = clock64();
+  for (int s = 0; s < world; ++s) {
+    for (;;) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(own + s) : "memory");
+      if (v - e >= 0) break;
+      if (clock64() - t0 > limit) {
+        if (atomicExch(&g_device_error, kErrGatherTimeout) == 0) {
+          g_device_error_info[0] = (int)blockIdx.x;
+          g_device_error_info[1] = s;
+          g_device_error_info[2] = v;
+          g_device_error_info[3] = e;
+        }
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
+__global__ void gather_sync_dev_kernel(FlagPtrs flags, int world, int rank, int* epoch_ctr, const int* own,
+                                       long long limit) {
+  signal_then_wait(flags, world, rank, epoch_ctr, own, limit);
+}
+
+// The token split's residual all-gather in one launch: every block copies
+// its share of this rank's rows to each destination, fences them and takes
+// a ticket; the last block to finish (all stores fenced before their
+// tickets) resets the ticket, raises this rank's epoch flag everywhere and
+// waits (bounded) for every rank's.
+__global__ void __launch_bounds__(256) rows_gather_dev_kernel(const uint4* __restrict__ src, DstPtrs dst, int n_dst,
+                                                              long long n16, FlagPtrs flags, int world, int rank,
+                                                              int* epoch_ctr, const int* own, long long limit,
+                                                              unsigned* ticket) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    const uint4 v = src[i];
+    for (int d = 0; d < n_dst; ++d) dst.p[d][i] = v;
+  }
+  __shared__ bool last;
+  __threadfence_system();  // every thread's peer stores, before the block's ticket
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  if (threadIdx.x == 0) *ticket = 0u;
+  __threadfence_system();
+  signal_then_wait(flags, world, rank, epoch_ctr, own, limit);
+}
+
 }  // namespace cevk
 
 using namespace cevk;
@@ -191,6 +256,46 @@ int cevk_gather_wait_dev(const int32_t* flags, int32_t world, const int32_t* epo
     return set_error(CEVK_E_SHAPE, "gather_wait_dev: world %d", world);
   gather_wait_dev_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, world, epoch, limit_cycles);
   return check_launch("gather_wait_dev_kernel");
+}
+
+int cevk_gather_sync_dev(int32_t* const* flags, int32_t world, int32_t rank, int32_t* epoch, const int32_t* own_flags,
+                         int64_t limit_cycles, void* stream) {
+  if (!flags || !epoch || !own_flags || world < 1 || world > kMaxRanks || rank < 0 || rank >= world ||
+      limit_cycles <= 0)
+    return set_error(CEVK_E_SHAPE, "gather_sync_dev: world %d rank %d", world, rank);
+  FlagPtrs f{};
+  for (int i = 0; i < world; ++i) {
+    if (!flags[i]) return set_error(CEVK_E_SHAPE, "gather_sync_dev: null flag array %d", i);
+    f.p[i] = flags[i];
+  }
+  gather_sync_dev_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(f, world, rank, epoch, own_flags,
+                                                                               limit_cycles);
+  return check_launch("gather_sync_dev_kernel");
+}
+
+int cevk_rows_gather_dev(const void* src, void* const* dst, int32_t n_dst, int64_t bytes, int32_t* const* flags,
+                         int32_t world, int32_t rank, int32_t* epoch, const int32_t* own_flags, int64_t limit_cycles,
+                         uint32_t* ticket, void* stream) {
+  if (!src || !dst || n_dst < 1 || n_dst > kMaxRanks || bytes < 0 || (bytes & 15) || ((uintptr_t)src & 15) ||
+      !flags || !epoch || !own_flags || !ticket || world < 1 || world > kMaxRanks || rank < 0 || rank >= world ||
+      limit_cycles <= 0)
+    return set_error(CEVK_E_SHAPE, "rows_gather_dev: %d destinations, %lld bytes, world %d", n_dst,
+                     (long long)bytes, world);
+  DstPtrs d{};
+  for (int i = 0; i < n_dst; ++i) {
+    if (!dst[i] || ((uintptr_t)dst[i] & 15)) return set_error(CEVK_E_SHAPE, "rows_gather_dev: destination %d", i);
+    d.p[i] = reinterpret_cast<uint4*>(dst[i]);
+  }
+  FlagPtrs f{};
+  for (int i = 0; i < world; ++i) {
+    if (!flags[i]) return set_error(CEVK_E_SHAPE, "rows_gather_dev: null flag array %d", i);
+    f.p[i] = flags[i];
+  }
+  const long long n16 = bytes / 16;
+  const long long blocks = std::max<long long>(1, std::min<long long>((n16 + 255) / 256, 148 * 8));
+  rows_gather_dev_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(src), d, n_dst, n16, f, world, rank, epoch, own_flags, limit_cycles, ticket);
+  return check_launch("rows_gather_dev_kernel");
 }
 
 int cevk_rows_to_peers(const void* src, void* const* dst, int32_t n_dst, int64_t bytes, void* stream) {

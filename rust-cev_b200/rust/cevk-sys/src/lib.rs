@@ -71,6 +71,11 @@ unsafe extern "C" {
                                 stream: *mut c_void) -> i32;
     pub fn cevk_rows_to_peers(src: *const c_void, dst: *const *mut c_void, n_dst: i32, bytes: i64,
                               stream: *mut c_void) -> i32;
+    pub fn cevk_gather_sync_dev(flags: *const *mut i32, world: i32, rank: i32, epoch: *mut i32,
+                                own_flags: *const i32, limit_cycles: i64, stream: *mut c_void) -> i32;
+    pub fn cevk_rows_gather_dev(src: *const c_void, dst: *const *mut c_void, n_dst: i32, bytes: i64,
+                                flags: *const *mut i32, world: i32, rank: i32, epoch: *mut i32, own_flags: *const i32,
+                                limit_cycles: i64, ticket: *mut u32, stream: *mut c_void) -> i32;
     pub fn cevk_qk_norm_rope(qkv: *const c_void, row_stride: i32, q_head_stride: i32, k_col: i32, v_col: i32,
                              q_norm_w: *const c_void, k_norm_w: *const c_void, eps: f32, norm_plus_one: i32,
                              pos: *const i32, theta: f64, rotary_dim: i32, q_out: *mut c_void,

@@ -80,9 +80,10 @@ def test_lfm2_kv_head_split_matches_unsplit():
 def _rank_fused(rank, world, port, q):
     """bf16: the split engine with the fused head gather (attention epilogue
     stores into every rank's buffer over NVLink) against the same split
-    engine with the NCCL all-gather: same kernels, same bits.  Likewise with
-    the token split (residual stream over NVLink peer stores vs NCCL), and
-    its prefill chunks replayed from CUDA graphs (device-side epochs)."""
+    engine with the NCCL all-gather: same kernels, same bits.  The token
+    split with the residual stream over NVLink peer stores agrees with the
+    NCCL token split to bf16 noise, and its prefill chunks replayed from
+    CUDA graphs (device-side epochs) match its eager chunks bit for bit."""
     import torch.distributed as dist
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -134,5 +135,8 @@ def test_lfm2_fused_head_gather_matches_nccl_gather():
     res = {v[0]: v[1:] for v in (q.get(timeout=10) for _ in range(2))}
     for r in (0, 1):
         err, err_ts, err_graph, err_split, epochs = res[r]
-        assert epochs > 0 and err == 0.0 and err_ts == 0.0 and err_graph == 0.0, res
-        assert err_split < 0.1, res  # token split vs not: same math, other GEMM shapes (bf16)
+        assert epochs > 0 and err == 0.0 and err_graph == 0.0, res
+        # token split vs not, and peer-store vs NCCL token split (the latter
+        # recomputes the conv tails on every rank, the former ships the conv
+        # kernel's): same math, other GEMM shapes (bf16)
+        assert err_split < 0.1 and err_ts < 0.1, res
