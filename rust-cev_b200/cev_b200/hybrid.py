@@ -194,7 +194,9 @@ class _HybridDecoder:
             if b > a:
                 xs = x[a:b]
                 hs = ops.add_rms_norm(xs, o, L["ln2"], self.eps, self.plus_one)
-                ops.residual_add(xs, F.linear(ops.swiglu(F.linear(hs, L["gu"])), L["down"]))
+                # the MLP's down projection accumulates into the residual rows
+                # (one GEMM with beta = 1 instead of a GEMM and an add)
+                xs.addmm_(ops.swiglu(F.linear(hs, L["gu"])), L["down"].t())
             if fused is not None:
                 x = fused.gather_rows(k, a, b + (K1 if conv_tail and ships_tails else 0), n)
                 k = 1 - k
