@@ -26,6 +26,12 @@ from .arena import KvArena, PrefixCache
 from .engine import InputError, Output, Readout, Request
 
 
+def dist_all_gather(out: torch.Tensor, t: torch.Tensor, split) -> None:
+    """Every rank's ``t`` into ``out`` (rank order), over the split's group."""
+    import torch.distributed as dist
+    dist.all_gather_into_tensor(out, t, group=split.group)
+
+
 @dataclass
 class HybridState:
     arena: KvArena | None
@@ -153,61 +159,95 @@ class _HybridDecoder:
         """The layer loop with a KV-head split over ranks: attention runs
         this rank's heads on every token (its head outputs gathered across
         ranks), everything token-local -- the output projection, the short
-        conv, the MLP, the norms -- runs only on this rank's token rows, and
-        one all-gather per layer rebuilds the residual stream on every rank
-        (NVLink peer stores into the fused gather's row buffers, or NCCL).
+        conv, the MLP, the norms -- runs only on this rank's token rows.
         A row batch splits by whole rows, a sequence chunk into contiguous
-        runs in rank order; a later run's short conv also runs over the K-1
-        tokens before it (their outputs are dropped), and with ``keep``
-        every rank recomputes the sequence's new conv tails from the
-        gathered stream, so every rank's state stays whole.  ``tails``:
-        (read, write) tail buffers by layer for a graph-captured chunk."""
+        runs in rank order.  The residual stream is all-gathered (NVLink
+        peer stores into the fused gather's row buffers, or NCCL) only
+        where every token is needed: before each attention layer and, for a
+        row batch, at the end.  Between gathers a run's short convs read
+        K-1 rows before it, so each layer before them also computes those
+        rows (recomputed from the last gathered stream; their outputs are
+        dropped once consumed).  With ``keep`` the rank that runs the
+        chunk's last token collects every conv layer's new tails (written
+        by its conv kernel) and one gather at the end gives them to every
+        rank; the returned stream then holds only this rank's rows.
+        ``tails``: (read, write) tail buffers by layer for a graph-captured
+        chunk."""
         sp = self.split
         n = B * T
         a, b, unit = self._token_runs(B, T)
         K1 = getattr(self, "K", 1) - 1
+        kinds = [L["kind"] for L in self.layers]
+        if any(k not in ("attn", "conv") for k in kinds):
+            raise NotImplementedError("token split: attention and short-conv layers only")
+        conv = [i for i, k in enumerate(kinds) if k == "conv"]
+        # rows before `a` each layer must also produce: the conv layers up to
+        # the next gather read K-1 more each (a row batch never crosses rows)
+        need = [0] * len(kinds)
+        if B == 1:
+            for i in range(len(kinds) - 2, -1, -1):
+                need[i] = need[i + 1] + K1 if kinds[i + 1] == "conv" else 0
         fused = sp.fused if sp.fused is not None and sp.fused.hidden == self.hidden else None
-        if fused is not None and n + K1 > fused.max_tokens:
-            raise ValueError(f"{n} tokens: the residual buffers hold {fused.max_tokens - K1}")
+        extra = len(conv) * K1 if keep else 0
+        if fused is not None and n + extra > fused.max_tokens:
+            raise ValueError(f"{n} tokens: the residual buffers hold {fused.max_tokens - extra}")
+        owner = keep and B == 1 and b == T and b > a
+        if keep:
+            # the owner's tails, one (K-1) x d block per conv layer (bytes of a
+            # [1, d, K-1] tail each): after the stream in residual buffer 0
+            if fused is not None:
+                stage = fused.rows[0][n:n + extra]
+            else:
+                stage = torch.empty(extra, self.hidden, dtype=self.dtype, device=self.device)
+        k = 0
         if fused is not None:
-            k = 0
             x = ops.embed(self.embed_w, ids, out=fused.rows[0][:n])
         else:
             x = ops.embed(self.embed_w, ids)
-        # With the peer-store gather, the rank that runs a sequence's last
-        # token writes each conv layer's new tails (d x (K-1) values) into
-        # the K-1 rows after the stream and sends them with its rows.
-        ships_tails = fused is not None and keep and b == T and b > a
+
+        def gather(x, k):
+            if fused is not None:
+                return fused.gather_rows(k, a, b, n), 1 - k
+            sp.gather_rows(x, a, b, unit)
+            return x, k
+
         for i, L in enumerate(self.layers):
-            conv_tail = L["kind"] == "conv" and keep and fused is not None
+            lo = min(b, max(0, a - need[i]))
             if L["kind"] == "attn":
+                if i > 0:
+                    x, k = gather(x, k)
                 h = ops.rms_norm(x, L["ln1"], self.eps, self.plus_one)
                 ctx = self._attn_ctx(i, L, h, pos_t, rows_t, plan)
-                o = F.linear(ctx[a:b], L["o"]) if b > a else None
-            elif L["kind"] == "conv":
-                dst = None
-                if conv_tail and ships_tails:
-                    dst = fused.rows[k][n:n + K1].reshape(-1)[:self.hidden * K1].view(1, self.hidden, K1)
-                o = self._conv_rows(i, L, x, a, b, B, T, state, keep and not conv_tail, tails, tail_dst=dst)
+                o = F.linear(ctx[lo:b], L["o"]) if b > lo else None
             else:
-                raise NotImplementedError("token split: attention and short-conv layers only")
-            if b > a:
-                xs = x[a:b]
+                dst = None
+                if owner:
+                    j = conv.index(i)
+                    dst = stage[j * K1:(j + 1) * K1].reshape(-1)[:self.hidden * K1].view(1, self.hidden, K1)
+                o = self._conv_rows(i, L, x, lo, b, B, T, state, tails, tail_dst=dst)
+            if b > lo:
+                xs = x[lo:b]
                 hs = ops.add_rms_norm(xs, o, L["ln2"], self.eps, self.plus_one)
                 # the MLP's down projection accumulates into the residual rows
-                # (one GEMM with beta = 1 instead of a GEMM and an add)
                 xs.addmm_(ops.swiglu(F.linear(hs, L["gu"])), L["down"].t())
-            if fused is not None:
-                x = fused.gather_rows(k, a, b + (K1 if conv_tail and ships_tails else 0), n)
-                k = 1 - k
-                if conv_tail:
-                    got = fused.rows[k][n:n + K1].reshape(-1)[:self.hidden * K1].view(1, self.hidden, K1)
-                    if tails is not None:
-                        tails[1][i].copy_(got)
-                    else:
-                        state.conv[i] = got.clone()
+        if not keep:
+            x, k = gather(x, k)
+            return x
+        # the chunk's tails from the rank that ran its last token to every rank
+        src = (T - 1) // unit
+        if fused is not None:
+            fused.gather_rows(0, n, n + (extra if owner else 0), n)
+            got = fused.rows[1][n:n + extra]
+        else:
+            allt = torch.empty(sp.world * extra, self.hidden, dtype=self.dtype, device=self.device)
+            dist_all_gather(allt, stage, sp)
+            got = allt[src * extra:(src + 1) * extra]
+        for j, i in enumerate(conv):
+            t = got[j * K1:(j + 1) * K1].reshape(-1)[:self.hidden * K1].view(1, self.hidden, K1)
+            if tails is not None:
+                tails[1][i].copy_(t)
             else:
-                sp.gather_rows(x, a, b, unit)
+                state.conv[i] = t.clone()
         return x
 
     def _attn_common(self, i, L, h, pos_t, rows_t, plan, q_cols, k_col, v_col, rot, attend=None):
@@ -360,43 +400,26 @@ class Lfm2(_HybridDecoder):
             state.conv[i] = tail_out
         return F.linear(y, L["out"])
 
-    def _conv_rows(self, i, L, x, a, b, B, T, state, keep, tails=None, tail_dst=None):
-        """ShortConv::forward (lfm2.rs:199-219) on token rows [a, b) of the
-        residual stream x [B*T, H]: whole rows continuing the state's tails
-        (B > 1), or a run of one sequence, computed over the K-1 tokens
-        before it too (their outputs are dropped) unless it starts the
-        sequence, where the state's tails precede it.  With ``keep`` every
-        rank derives the sequence's new tails (B * x of the in_proj output
-        of its last K-1 tokens, rounded to the model dtype as the conv
-        kernel rounds its inputs) from the same stream rows; ``tail_dst``
-        instead takes the tails the conv kernel writes for the run that
-        ends the sequence (the peer-store gather ships them)."""
+    def _conv_rows(self, i, L, x, lo, b, B, T, state, tails=None, tail_dst=None):
+        """ShortConv::forward (lfm2.rs:199-219) producing token rows [lo, b)
+        of the residual stream x [B*T, H]: whole rows continuing the state's
+        tails (B > 1), or rows of one sequence, for which the conv also runs
+        over the K-1 rows before lo (their outputs are dropped) unless it
+        starts at the sequence's first token, where the state's tails
+        precede it.  ``tail_dst``: where the conv kernel writes the
+        sequence's new tails (the run that ends the chunk)."""
         d, K = self.hidden, self.K
         tail_prev = tails[0][i] if tails is not None else (None if state is None else state.conv.get(i))
-        out = None
-        if b > a:
-            if B > 1:
-                bcx = F.linear(ops.rms_norm(x[a:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
-                y = ops.short_conv(bcx, (b - a) // T, T, d, L["conv_w"], L["bias"], tail_prev, None)
-                out = F.linear(y, L["out"])
-            else:
-                lo = max(0, a - (K - 1))
-                bcx = F.linear(ops.rms_norm(x[lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
-                y = ops.short_conv(bcx, 1, b - lo, d, L["conv_w"], L["bias"], tail_prev if a == 0 else None,
-                                   tail_dst)
-                out = F.linear(y[a - lo:], L["out"])
-        if keep:
-            lo = max(0, T - (K - 1))
-            hb = F.linear(ops.rms_norm(x[lo:T], L["ln1"], self.eps, self.plus_one), L["in_proj"])
-            cur = (hb[:, :d] * hb[:, 2 * d:]).t()
-            if T - lo < K - 1:  # a chunk shorter than the tail keeps part of the previous one
-                prev = tail_prev[0] if tail_prev is not None else torch.zeros(d, K - 1, dtype=x.dtype, device=x.device)
-                cur = torch.cat([prev[:, T - lo:], cur], 1)
-            if tails is not None:
-                tails[1][i][0].copy_(cur)
-            else:
-                state.conv[i] = cur.unsqueeze(0).contiguous()
-        return out
+        if b <= lo:
+            return None
+        if B > 1:
+            bcx = F.linear(ops.rms_norm(x[lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+            y = ops.short_conv(bcx, (b - lo) // T, T, d, L["conv_w"], L["bias"], tail_prev, None)
+            return F.linear(y, L["out"])
+        in_lo = max(0, lo - (K - 1))
+        bcx = F.linear(ops.rms_norm(x[in_lo:b], L["ln1"], self.eps, self.plus_one), L["in_proj"])
+        y = ops.short_conv(bcx, 1, b - in_lo, d, L["conv_w"], L["bias"], tail_prev if in_lo == 0 else None, tail_dst)
+        return F.linear(y[lo - in_lo:], L["out"])
 
 
 class ChunkGraphs:
