@@ -192,12 +192,16 @@ def test_cfg5_shape_served_probabilities_match_oracle():
     plen = 65536
     prefix, qs = workloads.decision_request(30_001, plen, 64, 64, 64, 4, cfg["vocab_size"] - 1)
     p = {}
-    for dt in (torch.bfloat16, torch.float32):
-        dec = hybrid.Lfm2(cfg, w_dev, dt, "cuda", max_len=plen + 1024, arena_rows=plen + 8192)
-        gpu = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=512, pass_tokens=8192, prefix_cache_tokens=plen)
+    for dt, graphs in ((torch.bfloat16, False), (torch.float32, False), ("graphs", True)):
+        dec = hybrid.Lfm2(cfg, w_dev, torch.bfloat16 if graphs else dt, "cuda", max_len=plen + 1024,
+                          arena_rows=plen + 8192)
+        gpu = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=512, pass_tokens=8192, prefix_cache_tokens=plen,
+                                  chunk_graphs=graphs)
         p[dt] = service.run_debiased(gpu, prefix, qs, "none", codes, workloads.SEP_ID)[1]
         del gpu, dec
         torch.cuda.empty_cache()
+    # the bench's path: the state's chunks replayed from CUDA graphs, bit for bit the eager chunks
+    assert all(torch.equal(torch.as_tensor(a), torch.as_tensor(b)) for a, b in zip(p["graphs"], p[torch.bfloat16]))
     r = {}
     with _OracleOn("cuda"):
         for dt in (torch.bfloat16, torch.float32):
