@@ -140,3 +140,64 @@ def test_lfm2_fused_head_gather_matches_nccl_gather():
         # recomputes the conv tails on every rank, the former ships the conv
         # kernel's): same math, other GEMM shapes (bf16)
         assert err_split < 0.1 and err_ts < 0.1, res
+
+
+def _rank_cfg5(rank, world, port, q):
+    """f32, cfg5 layer shapes: the KV-head split with the token split (NCCL
+    gathers) against the unsplit model, served probabilities."""
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=timedelta(seconds=120))
+    try:
+        from cev_b200 import configs, hybrid, service, weights, workloads
+        from cev_b200.tp import KvHeadSplit
+        cfg = configs.get("cfg5")
+        cfg["num_hidden_layers"] = 4
+        cfg["layer_types"] = ["conv", "conv", "full_attention", "conv"]
+        w = weights.init_weights(cfg, 3, torch.float32, f"cuda:{rank}")
+        codes = workloads.code_ids(4)
+        plen = 8192
+        prefix, qs = workloads.decision_request(30_002, plen, 16, 64, 64, 4, cfg["vocab_size"] - 1)
+
+        def served(split):
+            dec = hybrid.Lfm2(cfg, w, torch.float32, f"cuda:{rank}", max_len=plen + 1024, arena_rows=plen + 4096,
+                              split=split)
+            eng = hybrid.HybridEngine(dec, codes, pad_id=0, prefill_chunk=512, pass_tokens=8192,
+                                      prefix_cache_tokens=plen)
+            return torch.tensor(service.run_debiased(eng, prefix, qs, "none", codes, workloads.SEP_ID)[1])
+
+        D = cfg.get("head_dim") or cfg["hidden_size"] // cfg["num_attention_heads"]
+        sp = KvHeadSplit(cfg["num_attention_heads"], cfg["num_key_value_heads"], D, rank, world)
+        sp.sequence_parallel = True
+        got = served(sp)
+        err = None
+        if rank == 0:
+            err = (got - served(None)).abs().max().item()
+        dist.barrier()
+        q.put((rank, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_lfm2_token_split_cfg5_shape_served_probabilities():
+    """cfg5 layer shapes (hidden 2048, 32 Q / 8 KV heads, head_dim 64, conv
+    kernel 3; conv, conv, attention, conv), an 8192-token state in 512-token
+    chunks and 16 questions as right-padded rows, f32: the KV-head split with
+    the token-local layers on each rank's token rows serves the unsplit
+    model's probabilities within 5e-5."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank_cfg5, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+        assert p.exitcode == 0
+    res = dict(q.get(timeout=10) for _ in range(2))
+    assert res[0] is not None and res[0] < 5e-5, res
