@@ -23,9 +23,10 @@
 // TMEM per tile: S (BN f32 columns), a double buffer for P (bf16 packed in
 // pairs, BN/2 columns each) and the O accumulator (D f32 columns).  S_{j+1}
 // is issued as soon as the softmax has S_j in registers, so it runs while
-// block j is in softmax; P_j feeds the PV UMMA as the TMEM A operand, and
-// the softmax only waits for PV_{j-2} before reusing its P buffer (and for
-// PV_{j-1} before an O rescale).  Online softmax in the log2 domain; O is
+// block j is in softmax; P_j feeds the PV UMMA as the TMEM A operand.  The
+// S issuer commits S_j only after PV_{j-2} completed, so a softmax that has
+// S_j may overwrite PV_{j-2}'s P buffer without a wait of its own (it waits
+// for PV_{j-1} only before an O rescale).  Online softmax in the log2 domain; O is
 // only rescaled when a row max grows by more than 2^8 (values of P stay
 // <= 256, exact in f32 accumulation), which keeps TMEM traffic off the
 // common path.
@@ -300,6 +301,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           const uint64_t bd = umma_desc_sw128(sK(t, st) + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
           umma_bf16_ss(d, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
+        // s_full_j also stands for "PV_{j-2} completed", so the softmax can
+        // write P_j into PV_{j-2}'s buffer without a wait of its own: this
+        // thread observes o_done before the commit whose arrival the softmax
+        // waits for.  (PV_{j-2} completes during the softmax of block j-1,
+        // well before S_j is needed.  o_done[j&1] is not two phases ahead:
+        // PV_j needs P_j, which needs this commit; nor behind: PV_{j-4} was
+        // waited here for S_{j-2}.)
+        if (j >= 2) {
+          if (!mbar_wait(b_odone(t, j & 1), ((j - 2) >> 1) & 1, abort_flag)) break;
+          tc_fence_after();
+        }
         umma_commit(b_sfull(t));
         umma_commit(b_kempty(t, st));
         issued_any = true;
@@ -399,13 +411,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         pk[c >> 1] = pack_bf16x2(e0, e1);
       }
       const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
-      // P buffer j&1 is free once PV_{j-2} completed.  o_done[j&1] is not
-      // behind by a phase (PV_{j-4} was waited here two blocks ago) nor
-      // ahead (PV_j needs P_j).
-      if (j >= 2) {
-        if (!__all_sync(0xffffffffu, mbar_wait(b_odone(t, j & 1), ((j - 2) >> 1) & 1, abort_flag))) { ok = false; break; }
-        tc_fence_after();
-      }
+      // P buffer j&1 is free: PV_{j-2} completed before S_j was committed
+      // (the S issuer waits for it), and this thread observed s_full_j.
       if (__any_sync(0xffffffffu, factor != 1.f)) {
         // O is rescaled in TMEM: PV of the previous block must be done (and
         // PV of this block cannot start before P_j is signalled).
