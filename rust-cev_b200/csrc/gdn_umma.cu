@@ -574,18 +574,22 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
 // per TMEM lane quarter, each on 32 of the 64 columns) compute v_new, the
 // state and the output.  D1 alternates between two TMEM buffers by chunk,
 // so a chunk's output is read after the next chunk's products have started.
+// The chain from one chunk's state to the next is D1's W S rows -> v_new ->
+// D2 -> S: D2 commits on its own (s23) ahead of the intra v_new products
+// (out), which run while the epilogue updates the state, and the v_new
+// warps hold U in registers before D1 completes.
 constexpr int S_AWQ = 0;                  // [q'^T hi][W^T hi][q'^T lo][W^T lo], 128 d-rows x 64 tokens each
 constexpr int S_AK = S_AWQ + AWQ_B;       // [k' hi d0-63][k' hi d64-127][k' lo ..][..], 64 tokens x 64 d each
 constexpr int S_AI = S_AK + AK_B;         // [intra hi][0][intra lo][0]: two 128-row A tiles [intra; 0]
 constexpr int S_S = S_AI + 4 * T64;       // S hi, lo: 128 d-rows x 64 columns (MN-major B)
 constexpr int S_V = S_S + 2 * T128;       // v_new hi, lo: 64 tokens x 64 columns (MN-major B)
 constexpr int S_U = S_V + 2 * T64;        // U^T slice f32 [64 columns][64 tokens]
-constexpr int S_BAR = S_U + NS * C * 4;   // 9 mbarriers
-constexpr int S_MISC = S_BAR + 80;
+constexpr int S_BAR = S_U + NS * C * 4;   // 11 mbarriers
+constexpr int S_MISC = S_BAR + 96;
 constexpr int S_SMEM = S_MISC + 16;
 constexpr int EPI = 256;                  // epilogue threads
 constexpr int SCAN_THREADS = 64 + EPI;
-constexpr uint32_t REST_B = AK_B + AI_B + NS * C * 4;
+constexpr uint32_t REST_B = AK_B + NS * C * 4;  // k' images and the U^T slice
 constexpr int TM_D2 = 64;                 // D2 columns; D1 at 0 and 128 by chunk parity
 
 __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p) {
@@ -598,10 +602,12 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * NS, h = blockIdx.y, b = blockIdx.z;
   // awq_hi / awq_lo: the hi / lo planes of [q'^T; W^T] landed; s1a: the
-  // UMMAs reading the hi planes completed, s1: all of D1 = [q'; W] S
+  // UMMAs reading the hi planes completed, s1: all of D1 = [q'; W] S;
+  // rest: the k' images and U landed, ai: the intra images landed; s23: D2
+  // completed, out: D1 += [intra; 0] v_new completed
   const uint32_t bar_awq = sb + S_BAR, bar_rest = bar_awq + 8, bar_s1 = bar_awq + 16, bar_s23 = bar_awq + 24,
                  bar_vnew = bar_awq + 32, bar_sready = bar_awq + 40, bar_drain = bar_awq + 48,
-                 bar_awq_lo = bar_awq + 56, bar_s1a = bar_awq + 64;
+                 bar_awq_lo = bar_awq + 56, bar_s1a = bar_awq + 64, bar_ai = bar_awq + 72, bar_out = bar_awq + 80;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S_MISC + 4);
   const int nc = p.n_chunks;
@@ -616,6 +622,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
     mbar_init(bar_vnew, EPI / 32);  // one arrival per epilogue warp
     mbar_init(bar_sready, EPI / 32);
     mbar_init(bar_drain, 1);
+    mbar_init(bar_ai, 1);
+    mbar_init(bar_out, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -631,7 +639,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- operand loads ----------------
-      int n_awq = 0, n_lo = 0, n_rest = 0;  // copies issued on each barrier
+      int n_awq = 0, n_lo = 0, n_rest = 0, n_ai = 0;  // copies issued on each barrier
       for (int c = 0; c < nc; ++c) {
         const uint8_t* rec = p.rec + chunk_index(p, b, c, h) * REC_B;
         // hi planes once the previous chunk's UMMAs reading them are done,
@@ -646,20 +654,26 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
 #pragma unroll
         for (int k = 4; k < 8; ++k) bulk_g2s(sb + S_AWQ + k * T64, rec + k * T64, T64, bar_awq_lo);
         ++n_lo;
+        // k' and U once the previous chunk's D2 is done (U was read before
+        // D2 was issued), intra once its intra products are
         if (c > 0 && !mbar_wait(bar_s23, (c - 1) & 1, abort_flag, WAIT)) break;
         mbar_arrive_expect_tx(bar_rest, REST_B);
         bulk_g2s(sb + S_AK, rec + AWQ_B, AK_B / 2, bar_rest);
         bulk_g2s(sb + S_AK + AK_B / 2, rec + AWQ_B + AK_B / 2, AK_B / 2, bar_rest);
-        bulk_g2s(sb + S_AI, rec + AWQ_B + AK_B, T64, bar_rest);
-        bulk_g2s(sb + S_AI + 2 * T64, rec + AWQ_B + AK_B + T64, T64, bar_rest);
         bulk_g2s(sb + S_U, rec + AWQ_B + AK_B + AI_B + (size_t)n0 * C * 4, NS * C * 4, bar_rest);
         ++n_rest;
+        if (c > 0 && !mbar_wait(bar_out, (c - 1) & 1, abort_flag, WAIT)) break;
+        mbar_arrive_expect_tx(bar_ai, AI_B);
+        bulk_g2s(sb + S_AI, rec + AWQ_B + AK_B, T64, bar_ai);
+        bulk_g2s(sb + S_AI + 2 * T64, rec + AWQ_B + AK_B + T64, T64, bar_ai);
+        ++n_ai;
       }
       // drain: every copy has landed before the CTA exits
       volatile int never = 0;
       if (n_awq > 0) mbar_wait(bar_awq, (n_awq - 1) & 1, &never, WAIT);
       if (n_lo > 0) mbar_wait(bar_awq_lo, (n_lo - 1) & 1, &never, WAIT);
       if (n_rest > 0) mbar_wait(bar_rest, (n_rest - 1) & 1, &never, WAIT);
+      if (n_ai > 0) mbar_wait(bar_ai, (n_ai - 1) & 1, &never, WAIT);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -705,14 +719,22 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
           umma_bf16_ss(tmem + TM_D2, kh, vh, id_mnmn, s > 0 ? 1u : 0u);
           umma_bf16_ss(tmem + TM_D2, kh, vl, id_mnmn, 1u);
           umma_bf16_ss(tmem + TM_D2, kl, vh, id_mnmn, 1u);
+        }
+        umma_commit(bar_s23);
+        if (!mbar_wait(bar_ai, c & 1, abort_flag, WAIT)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < C / 16; ++s) {
           // D1 += [intra; 0] v_new (A K-major)
+          const uint64_t vh = umma_desc_sw128(sb + S_V + s * 2048, T64, 1024);
+          const uint64_t vl = umma_desc_sw128(sb + S_V + T64 + s * 2048, T64, 1024);
           const uint64_t ih = umma_desc_sw128(sb + S_AI + s * 32, 16, 1024);
           const uint64_t il = umma_desc_sw128(sb + S_AI + 2 * T64 + s * 32, 16, 1024);
           umma_bf16_ss(d1, ih, vh, id_kmn, 1u);
           umma_bf16_ss(d1, ih, vl, id_kmn, 1u);
           umma_bf16_ss(d1, il, vh, id_kmn, 1u);
         }
-        umma_commit(bar_s23);
+        umma_commit(bar_out);
       }
       if (any) {  // every UMMA issued has completed before TMEM is freed
         umma_commit(bar_drain);
@@ -756,6 +778,12 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
     for (; c < nc; ++c) {
       const uint32_t d1 = (c & 1) * 128;
       const float el = p.elast[chunk_index(p, b, c, h)];
+      float u[32];  // U for token r - 64 (v_new rows), loaded while D1 runs
+      if (r >= C) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_rest, c & 1, abort_flag, WAIT))) break;
+#pragma unroll
+        for (int n = 0; n < 32; ++n) u[n] = sU[(c0 + n) * C + r - C];
+      }
       if (!__all_sync(0xffffffffu, mbar_wait(bar_s1, c & 1, abort_flag, WAIT))) break;
       tc_fence_after();
       if (r >= C) {  // v_new = U - W S for token r - 64
@@ -763,12 +791,11 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
         float ws[32];
         tmem_ld32(tl + d1 + c0, ws);
         tmem_wait_ld();
-        if (!__all_sync(0xffffffffu, mbar_wait(bar_rest, c & 1, abort_flag, WAIT))) break;
 #pragma unroll
         for (int n8 = 0; n8 < 32; n8 += 8) {
           float f[8];
 #pragma unroll
-          for (int x = 0; x < 8; ++x) f[x] = sU[(c0 + n8 + x) * C + i] - ws[n8 + x];
+          for (int x = 0; x < 8; ++x) f[x] = u[n8 + x] - ws[n8 + x];
           uint4 hv, lv;
           split8(f, hv, lv);
           *reinterpret_cast<uint4*>(smem + S_V + sw(i, c0 + n8)) = hv;
@@ -793,6 +820,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sready);
       if (r < C) {  // out = q' S + intra v_new for token r (this chunk's D1 buffer)
+        if (!__all_sync(0xffffffffu, mbar_wait(bar_out, c & 1, abort_flag, WAIT))) break;
+        tc_fence_after();
         tmem_ld32(tl + d1 + c0, d2);
         tmem_wait_ld();
         const int t = c * C + r;
