@@ -316,6 +316,15 @@ static void launch_gated_norm(const float* core, const T* z, int z_rs, const T* 
   }
 }
 
+// The bf16 gated norm of rows [t0, t0 + rows) of a single-row call (the
+// pieces of gdn_umma.cu launch it piece by piece on their own stream).
+void gdn_gated_norm_rows_bf16(const float* core, const void* z, int z_rs, const void* w, float eps, void* y,
+                              long long t0, long long rows, int nv, int dv, cudaStream_t st) {
+  launch_gated_norm<__nv_bfloat16>(core + t0 * nv * dv, reinterpret_cast<const __nv_bfloat16*>(z) + t0 * z_rs, z_rs,
+                                   reinterpret_cast<const __nv_bfloat16*>(w), eps,
+                                   reinterpret_cast<__nv_bfloat16*>(y) + t0 * nv * dv, rows, nv, dv, st);
+}
+
 static size_t gdn_smem(int dk) {
   const int KP = dk + 1;
   return sizeof(float) * (3 * GC * KP + 2 * GC * (GC + 1) + GC * GDVS + dk * GDVS + 3 * GC);
@@ -326,7 +335,7 @@ bool gdn_tc_supported(int dk, int dv);
 size_t gdn_umma_extra_floats(int B, int T, int nv);
 int gdn_umma_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
                  const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv,
-                 cudaStream_t st);
+                 const void* z, int z_rs, const void* norm_w, float eps, void* y, cudaStream_t st);
 int gdn_tc_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
                const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv, int dk,
                int dv, cudaStream_t st);
@@ -399,8 +408,10 @@ int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int3
     if (full_ws && aligned && dk == 128 && dv == 128) {
       // tcgen05 UMMA with TMEM accumulators (gdn_umma.cu): chunk-parallel
       // prep + state scan
+      // prep + state scan, and the gated norm
       rc = gdn_umma_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,
-                        nk, nv, st);
+                        nk, nv, z, z_row_stride, norm_w, eps, y, st);
+      return rc ? rc : check_launch("gdn_gated_norm_kernel");
     } else if (full_ws && aligned && gdn_tc_supported(dk, dv)) {
       // mma.sync (gdn_tc.cu), dk = dv = 64
       rc = gdn_tc_run(conv_out, C, ab, ab_row_stride, a_log, dt_bias, s_in, s_batch_stride, s_out, prm.core, B, T,

@@ -36,6 +36,10 @@
 //   UT   U^T f32 [dv][64]
 // 144 KB per (chunk, head, row): the size of the f32 workspace the host
 // sizes with cevk_gdn_workspace_size().
+#include <algorithm>
+#include <deque>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace cevk {
@@ -51,6 +55,7 @@ constexpr int T64 = 64 * 128;    // bytes of a 64-row tile
 constexpr uint32_t AWQ_B = 4 * T128, AK_B = 4 * T64, AI_B = 2 * T64, UT_B = DV * C * 4;
 constexpr size_t REC_B = (size_t)AWQ_B + AK_B + AI_B + UT_B;  // 147456
 constexpr long long WAIT = 1ll << 30;
+constexpr int PIECE = 21;  // chunks per piece of a long single-row call
 
 // Byte offset of (row r, column c < 64) in a 128-byte-swizzled tile of
 // 64-element bf16 rows: 16-byte chunk c/8 of row r sits at chunk (c/8) ^ (r%8).
@@ -86,6 +91,7 @@ struct Params {
   uint8_t* rec;      // per (row, chunk, head): REC_B bytes
   float* elast;      // per (row, chunk, head)
   int B, T, nk, nv, n_chunks;
+  int c0, c1;        // the chunks [c0, c1) this launch runs (prep: c0 + blockIdx.x)
 };
 
 __host__ __device__ inline size_t chunk_index(const Params& p, int b, int ch, int h) {
@@ -169,7 +175,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
     return;
   }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ch = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int ch = p.c0 + blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h / (p.nv / p.nk);  // key head read by this value head (qwen35.rs:436-441)
   const int t0 = ch * C;
   const int key_dim = p.nk * DK;
@@ -438,20 +444,33 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
     // ---- warps 4-7: q'^T rows (q' = q e^cum) and k' (k e^(last - cum)) ----
     const int u = tid - 128;
     // q'^T image rows d (128) x 8 chunks of 8 tokens: a warp stores 4 rows
-    // x 128 bytes, contiguous
+    // x 128 bytes, contiguous.  The eight lanes of one row d read tokens t8
+    // + x in an order rotated by the lane's t8 group, so that each read hits
+    // eight different swizzle chunks (rows t8 + x share their chunk, and
+    // hence their banks, for a fixed x); the values are rotated back after.
+    const int rot = u & 7;
 #pragma unroll 1
     for (int e = u; e < DK * 8; e += 128) {
       const int d = e >> 3, t8 = (e & 7) * 8;
       const uint8_t* th = smem + P_KQ + (d >> 6) * T128;
       const uint8_t* tl = th + 2 * T128;
-      float f[8];
+      float g[8];  // g[x]: token t8 + ((x + rot) & 7)
 #pragma unroll
       for (int x = 0; x < 8; ++x) {
-        const uint32_t o = sw(64 + t8 + x, d & 63);
+        const int xr = (x + rot) & 7;
+        const uint32_t o = sw(64 + t8 + xr, d & 63);
         const float q = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(th + o)) +
                         __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tl + o));
-        f[x] = q * sEq[t8 + x];
+        g[x] = q * sEq[t8 + xr];
       }
+      // f[y] = g[(y - rot) & 7], a barrel rotation with constant indices
+      float f[8];
+#pragma unroll
+      for (int y = 0; y < 8; ++y) f[y] = (rot & 4) ? g[(y + 4) & 7] : g[y];
+#pragma unroll
+      for (int y = 0; y < 8; ++y) g[y] = (rot & 2) ? f[(y + 6) & 7] : f[y];
+#pragma unroll
+      for (int y = 0; y < 8; ++y) f[y] = (rot & 1) ? g[(y + 7) & 7] : g[y];
       uint4 hv, lv;
       split8(f, hv, lv);
       *reinterpret_cast<uint4*>(rec + sw(d, t8)) = hv;             // q'^T hi
@@ -610,7 +629,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
                  bar_awq_lo = bar_awq + 56, bar_s1a = bar_awq + 64, bar_ai = bar_awq + 72, bar_out = bar_awq + 80;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + S_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S_MISC + 4);
-  const int nc = p.n_chunks;
+  const int nc = p.c1 - p.c0;  // chunk c of the loops below is chunk p.c0 + c
 
   if (tid == 0) {
     mbar_init(bar_awq, 1);
@@ -641,7 +660,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
       // ---------------- operand loads ----------------
       int n_awq = 0, n_lo = 0, n_rest = 0, n_ai = 0;  // copies issued on each barrier
       for (int c = 0; c < nc; ++c) {
-        const uint8_t* rec = p.rec + chunk_index(p, b, c, h) * REC_B;
+        const uint8_t* rec = p.rec + chunk_index(p, b, p.c0 + c, h) * REC_B;
         // hi planes once the previous chunk's UMMAs reading them are done,
         // lo planes once all of its D1 products are
         if (c > 0 && !mbar_wait(bar_s1a, (c - 1) & 1, abort_flag, WAIT)) break;
@@ -777,7 +796,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
     int c = 0;
     for (; c < nc; ++c) {
       const uint32_t d1 = (c & 1) * 128;
-      const float el = p.elast[chunk_index(p, b, c, h)];
+      const float el = p.elast[chunk_index(p, b, p.c0 + c, h)];
       float u[32];  // U for token r - 64 (v_new rows), loaded while D1 runs
       if (r >= C) {
         if (!__all_sync(0xffffffffu, mbar_wait(bar_rest, c & 1, abort_flag, WAIT))) break;
@@ -824,7 +843,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
         tc_fence_after();
         tmem_ld32(tl + d1 + c0, d2);
         tmem_wait_ld();
-        const int t = c * C + r;
+        const int t = (p.c0 + c) * C + r;
         if (t < p.T) {
           float4* o = reinterpret_cast<float4*>(p.core + (((size_t)b * p.T + t) * p.nv + h) * DV + n0 + c0);
 #pragma unroll
@@ -847,6 +866,125 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
 
 }  // namespace gum
 
+namespace {
+
+// A long single-row call (a state run once through the layer) leaves most
+// SMs idle during its scan: 2 CTAs per value head, one per SM.  It runs in
+// pieces of PIECE chunks instead, the prep of piece i + 1 on the SMs the scan
+// of piece i leaves free: scans on a high-priority stream, preps on a
+// low-priority one, the state carried from piece to piece through s_out.  A
+// prep runs at most two pieces ahead of the scans (piece i's prep waits for
+// the scan of piece i - 2), so that a freed SM goes to the next scan first.
+// The gated norm of each piece runs on a third stream once its scan is done
+// (it needs no shared memory, so it shares SMs with the preps and scans).
+// The streams fork from and join back into the caller's stream.
+struct PieceStreams {
+  int dev;
+  cudaStream_t scan, prep, norm;
+  std::deque<cudaEvent_t> ev;
+};
+std::mutex g_piece_mu;
+std::deque<PieceStreams> g_piece;
+
+// The calling thread holds g_piece_mu.
+int piece_streams(PieceStreams** out) {
+  int dev = 0, lo = 0, hi = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess)
+    for (PieceStreams& s : g_piece)
+      if (s.dev == dev) {
+        *out = &s;
+        return CEVK_OK;
+      }
+  PieceStreams s;
+  s.dev = dev;
+  if (e == cudaSuccess) e = cudaDeviceGetStreamPriorityRange(&lo, &hi);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&s.scan, cudaStreamNonBlocking, hi);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&s.prep, cudaStreamNonBlocking, lo);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&s.norm, cudaStreamNonBlocking, lo);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "gdn pieces: streams: %s", cudaGetErrorString(e));
+  g_piece.push_back(s);
+  *out = &g_piece.back();
+  return CEVK_OK;
+}
+
+int piece_event(PieceStreams& s, size_t i, cudaEvent_t* out) {
+  while (s.ev.size() <= i) {
+    cudaEvent_t x;
+    cudaError_t e = cudaEventCreateWithFlags(&x, cudaEventDisableTiming);
+    if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "gdn pieces: event: %s", cudaGetErrorString(e));
+    s.ev.push_back(x);
+  }
+  *out = s.ev[i];
+  return CEVK_OK;
+}
+
+}  // namespace
+
+struct GdnNorm {
+  const void* z;
+  int z_rs;
+  const void* w;
+  float eps;
+  void* y;
+};
+void gdn_gated_norm_rows_bf16(const float* core, const void* z, int z_rs, const void* w, float eps, void* y,
+                              long long t0, long long rows, int nv, int dv, cudaStream_t st);
+
+// Event slots: 0 the fork, 1 + 2 i the prep of piece i, 2 + 2 i its scan,
+// the last slot the last norm.
+int gdn_umma_pieces(const gum::Params& p0, const GdnNorm& nm, cudaStream_t st) {
+  std::lock_guard<std::mutex> lock(g_piece_mu);
+  PieceStreams* ps = nullptr;
+  int rc = piece_streams(&ps);
+  if (rc) return rc;
+  const int n = (p0.n_chunks + gum::PIECE - 1) / gum::PIECE;
+  cudaEvent_t fork, last_prep = nullptr, last_scan = nullptr, last_norm = nullptr, norm_done;
+  if ((rc = piece_event(*ps, 0, &fork)) || (rc = piece_event(*ps, 1 + 2 * n, &norm_done))) return rc;
+  cudaError_t e = cudaEventRecord(fork, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ps->prep, fork, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ps->scan, fork, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ps->norm, fork, 0);
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "gdn pieces: fork: %s", cudaGetErrorString(e));
+  for (int i = 0; i < n && !rc; ++i) {
+    gum::Params p = p0;
+    p.c0 = i * gum::PIECE;
+    p.c1 = std::min(p0.n_chunks, p.c0 + gum::PIECE);
+    if (i > 0) {  // continue the state the previous piece wrote
+      p.s_in = p0.s_out;
+      p.s_bs = 0;
+    }
+    cudaEvent_t ep, es, es2;
+    if ((rc = piece_event(*ps, 1 + 2 * i, &ep)) || (rc = piece_event(*ps, 2 + 2 * i, &es))) break;
+    if (i >= 2) {
+      if ((rc = piece_event(*ps, 2 * i - 2, &es2))) break;
+      if ((e = cudaStreamWaitEvent(ps->prep, es2, 0)) != cudaSuccess) break;
+    }
+    gum::gdn_umma_prep_kernel<<<dim3(p.c1 - p.c0, p.nv, 1), gum::PREP_THREADS, gum::P_SMEM, ps->prep>>>(p);
+    if ((rc = check_launch("gdn_umma_prep_kernel"))) break;
+    if ((e = cudaEventRecord(ep, ps->prep)) != cudaSuccess) break;
+    last_prep = ep;
+    if ((e = cudaStreamWaitEvent(ps->scan, ep, 0)) != cudaSuccess) break;
+    gum::gdn_umma_scan_kernel<<<dim3(gum::DV / gum::NS, p.nv, 1), gum::SCAN_THREADS, gum::S_SMEM, ps->scan>>>(p);
+    if ((rc = check_launch("gdn_umma_scan_kernel"))) break;
+    if ((e = cudaEventRecord(es, ps->scan)) != cudaSuccess) break;
+    last_scan = es;
+    if ((e = cudaStreamWaitEvent(ps->norm, es, 0)) != cudaSuccess) break;
+    const long long t0 = (long long)p.c0 * gum::C, t1 = std::min((long long)p.c1 * gum::C, (long long)p.T);
+    gdn_gated_norm_rows_bf16(p.core, nm.z, nm.z_rs, nm.w, nm.eps, nm.y, t0, t1 - t0, p.nv, gum::DV, ps->norm);
+    if ((rc = check_launch("gdn_gated_norm_kernel"))) break;
+    if ((e = cudaEventRecord(norm_done, ps->norm)) != cudaSuccess) break;
+    last_norm = norm_done;
+  }
+  // join: the caller's stream waits for everything enqueued above
+  if (last_prep && cudaStreamWaitEvent(st, last_prep, 0) != cudaSuccess && e == cudaSuccess) e = cudaErrorUnknown;
+  if (last_scan && cudaStreamWaitEvent(st, last_scan, 0) != cudaSuccess && e == cudaSuccess) e = cudaErrorUnknown;
+  if (last_norm && cudaStreamWaitEvent(st, last_norm, 0) != cudaSuccess && e == cudaSuccess) e = cudaErrorUnknown;
+  if (rc) return rc;
+  if (e != cudaSuccess) return set_error(CEVK_E_CUDA, "gdn pieces: %s", cudaGetErrorString(e));
+  return CEVK_OK;
+}
+
 // Workspace floats of the tcgen05 path beyond the core output: one operand
 // record per (row, chunk, value head) plus e^last.
 size_t gdn_umma_extra_floats(int B, int T, int nv) {
@@ -854,9 +992,14 @@ size_t gdn_umma_extra_floats(int B, int T, int nv) {
   return (size_t)B * nc * nv * (gum::REC_B / sizeof(float) + 1);
 }
 
+void gdn_gated_norm_rows_bf16(const float* core, const void* z, int z_rs, const void* w, float eps, void* y,
+                              long long t0, long long rows, int nv, int dv, cudaStream_t st);
+
+// Runs the delta rule into the f32 core output and the gated norm from it
+// into y.
 int gdn_umma_run(const void* conv_out, int C_, const void* ab, int ab_rs, const float* a_log, const float* dt_bias,
                  const float* s_in, long long s_bs, float* s_out, float* workspace, int B, int T, int nk, int nv,
-                 cudaStream_t st) {
+                 const void* z, int z_rs, const void* norm_w, float eps, void* y, cudaStream_t st) {
   gum::Params p;
   p.conv = reinterpret_cast<const __nv_bfloat16*>(conv_out);
   p.Cc = C_;
@@ -878,14 +1021,22 @@ int gdn_umma_run(const void* conv_out, int C_, const void* ab, int ab_rs, const 
   x = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(x) + 15) & ~uintptr_t(15));
   p.rec = x;
   p.elast = reinterpret_cast<float*>(x + (size_t)B * p.n_chunks * nv * gum::REC_B);
+  p.c0 = 0;
+  p.c1 = p.n_chunks;
   int rc;
   if ((rc = opt_in_smem((const void*)gum::gdn_umma_prep_kernel, gum::P_SMEM, "gdn_umma_prep_kernel")) ||
       (rc = opt_in_smem((const void*)gum::gdn_umma_scan_kernel, gum::S_SMEM, "gdn_umma_scan_kernel")))
     return rc;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (B == 1 && s_out && p.n_chunks >= 2 * gum::PIECE && cudaStreamIsCapturing(st, &cap) == cudaSuccess &&
+      cap == cudaStreamCaptureStatusNone)
+    return gdn_umma_pieces(p, GdnNorm{z, z_rs, norm_w, eps, y}, st);
   gum::gdn_umma_prep_kernel<<<dim3(p.n_chunks, nv, B), gum::PREP_THREADS, gum::P_SMEM, st>>>(p);
   if ((rc = check_launch("gdn_umma_prep_kernel"))) return rc;
   gum::gdn_umma_scan_kernel<<<dim3(gum::DV / gum::NS, nv, B), gum::SCAN_THREADS, gum::S_SMEM, st>>>(p);
-  return check_launch("gdn_umma_scan_kernel");
+  if ((rc = check_launch("gdn_umma_scan_kernel"))) return rc;
+  gdn_gated_norm_rows_bf16(p.core, z, z_rs, norm_w, eps, y, 0, (long long)B * T, nv, gum::DV, st);
+  return CEVK_OK;
 }
 
 }  // namespace cevk

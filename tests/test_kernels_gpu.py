@@ -347,6 +347,31 @@ def test_gdn_chunk_prefill_matches_oracle(dtype, tol, B, T, with_state, ws_kind,
     assert close(s_out, want_s, 1e-3 if rel else tol, rel)
 
 
+@pytest.mark.parametrize("T,with_state", [(2700, True), (4000, False)])
+def test_gdn_long_single_row_runs_in_pieces(T, with_state):
+    """A single-row bf16 call of 43+ chunks (dk = dv = 128) runs its prep
+    and scan in pieces on two streams, the state carried through s_out: the
+    same output bit for bit as the one-launch path (taken when s_out is not
+    asked for), and the oracle's within the chunked-prefill tolerance.
+    T = 4000 ends in a partial chunk."""
+    from cev_b200 import ops
+    B, nk, nv, dk, dv = 1, 2, 4, 128, 128
+    conv_out, ab, z, a_log, dt_bias, norm_w, s0 = gdn_inputs(B, T, nk, nv, dk, dv, torch.bfloat16, 12)
+    s_in = s0.cuda() if with_state else None
+    args = (conv_out.reshape(T, -1).cuda(), ab.reshape(T, -1).cuda(), 2 * nv, z.reshape(T, -1).cuda(), nv * dv,
+            a_log.cuda(), dt_bias.cuda(), norm_w.cuda(), 1e-6, s_in)
+    ws = torch.empty(ops.gdn_workspace_size(B, T, nv, dk, dv), dtype=torch.uint8, device="cuda")
+    s_out = torch.full((B, nv, dk, dv), float("nan"), device="cuda")
+    y = ops.gdn_chunk_prefill(*args, s_out, B, T, nk, nv, dk, dv, ws)
+    y_one = ops.gdn_chunk_prefill(*args, None, B, T, nk, nv, dk, dv, ws)
+    torch.cuda.synchronize()
+    ops.device_status()
+    assert torch.equal(y, y_one)
+    want_y, want_s = gdn_oracle(conv_out, ab, z, a_log, dt_bias, norm_w, s0 if with_state else None, nk, nv, dk, dv)
+    assert close(y.reshape(B, T, -1), want_y, 1e-2, True)
+    assert close(s_out, want_s, 1e-3, True)
+
+
 @pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 1e-2), (torch.float32, 1e-5)])
 def test_gdn_conv_matches_oracle(dtype, tol):
     from cev_b200 import ops
