@@ -323,18 +323,22 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
       tmem_wait_ld();
     }
     // decay e^(cum_i - cum_j) <= 1 for j <= i (the exponent is a sum of
-    // log-decays, never positive); __expf's error is relative to the value
+    // log-decays, never positive); __expf's error is relative to the value.
+    // Every element is computed and then masked (the exponent clamped at 0
+    // so that the masked-out ones stay finite): a lane-dependent condition
+    // around the exponential would split the warp at every column.
     if (r < C) {
       const int i = r;
       const float ci_ = sG[i], bi = sB[i];
 #pragma unroll
       for (int j4 = 0; j4 < C; j4 += 4) {
-        float4 a;
-        a.x = j4 + 0 < i ? bi * v[j4 + 0] * __expf(ci_ - sG[j4 + 0]) : 0.f;
-        a.y = j4 + 1 < i ? bi * v[j4 + 1] * __expf(ci_ - sG[j4 + 1]) : 0.f;
-        a.z = j4 + 2 < i ? bi * v[j4 + 2] * __expf(ci_ - sG[j4 + 2]) : 0.f;
-        a.w = j4 + 3 < i ? bi * v[j4 + 3] * __expf(ci_ - sG[j4 + 3]) : 0.f;
-        *reinterpret_cast<float4*>(sA + i * AP + j4) = a;
+        float a[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const float e = __expf(fminf(ci_ - sG[j4 + x], 0.f));
+          a[x] = (bi * v[j4 + x]) * (j4 + x < i ? e : 0.f);
+        }
+        *reinterpret_cast<float4*>(sA + i * AP + j4) = make_float4(a[0], a[1], a[2], a[3]);
       }
     } else {
       // intra rows into the (not yet used) T area, then out coalesced
@@ -344,7 +348,10 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
       for (int c8 = 0; c8 < C; c8 += 8) {
         float f[8];
 #pragma unroll
-        for (int x = 0; x < 8; ++x) f[x] = (c8 + x) <= i ? v[c8 + x] * __expf(ci_ - sG[c8 + x]) : 0.f;
+        for (int x = 0; x < 8; ++x) {
+          const float e = __expf(fminf(ci_ - sG[c8 + x], 0.f));
+          f[x] = v[c8 + x] * ((c8 + x) <= i ? e : 0.f);
+        }
         uint4 hv, lv;
         split8(f, hv, lv);
         *reinterpret_cast<uint4*>(smem + P_T + sw(i, c8)) = hv;
