@@ -370,23 +370,17 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
     //      substitution (warp w: diagonal block w, two lanes per column) ----
     {
       // lane c < 16 holds column c of the block's inverse in registers:
-      // t_i = [i == c] - sum_{j < i} A_ij t_j (t_j = 0 above the diagonal)
+      // t_i = [i == c] - sum_{j < i} A_ij t_j (t_j = 0 above the diagonal),
+      // accumulated column by column (once t_j is final it updates every
+      // t_i below it), so the dependent chain is one FMA per row
       const int b0 = warp * 16, c = lane & 15;
       float t[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float4* ar = reinterpret_cast<const float4*>(sA + (b0 + i) * AP + b0);
-        float acc = 0.f;
+      for (int i = 0; i < 16; ++i) t[i] = i == c ? 1.f : 0.f;
 #pragma unroll
-        for (int j4 = 0; j4 < i; j4 += 4) {
-          const float4 a = ar[j4 >> 2];
-          if (j4 + 0 < i) acc = fmaf(a.x, t[j4 + 0], acc);
-          if (j4 + 1 < i) acc = fmaf(a.y, t[j4 + 1], acc);
-          if (j4 + 2 < i) acc = fmaf(a.z, t[j4 + 2], acc);
-          if (j4 + 3 < i) acc = fmaf(a.w, t[j4 + 3], acc);
-        }
-        t[i] = i == c ? 1.f : (i < c ? 0.f : -acc);
-      }
+      for (int j = 0; j < 15; ++j)
+#pragma unroll
+        for (int i = j + 1; i < 16; ++i) t[i] = fmaf(-sA[(b0 + i) * AP + b0 + j], t[j], t[i]);
       if (lane < 16)
 #pragma unroll
         for (int i = 0; i < 16; ++i) sT[(b0 + i) * AP + b0 + c] = t[i];
