@@ -239,16 +239,47 @@ __global__ void __launch_bounds__(256, 3) qk_norm_rope_rows_kernel(
   const int sub = lane / L, d0 = (lane % L) * 8, half = rot / 2;
   const float p = (float)pos[t];
   float c[8], s[8];
+  if constexpr (D <= 128) {
+    // the warp's lanes each take 1 (D 64) or 2 (D 128) of the token's rot/2
+    // frequencies and hand the cos / sin out by shuffles: a lane needs 8
+    // of them, and each is needed by every lane pair (d, d + rot/2) of
+    // every head row in the warp
+    constexpr int NF = D / 64;
+    float cf[NF], sf[NF];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const int d = d0 + e;
-    c[e] = 1.f;
-    s[e] = 0.f;
-    if (d < rot) {
-      float sn, cs;
-      sincosf(p * inv.v[d < half ? d : d - half], &sn, &cs);
-      c[e] = cs;
-      s[e] = d < half ? -sn : sn;
+    for (int k = 0; k < NF; ++k) {
+      const int fi = lane + 32 * k;
+      cf[k] = 1.f;
+      sf[k] = 0.f;
+      if (fi < half) sincosf(p * inv.v[fi], &sf[k], &cf[k]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int d = d0 + e, f = d < half ? d : d - half;
+      float cs = 1.f, sn = 0.f;
+#pragma unroll
+      for (int k = 0; k < NF; ++k) {
+        const float a = __shfl_sync(0xffffffffu, cf[k], f & 31), b = __shfl_sync(0xffffffffu, sf[k], f & 31);
+        if ((f >> 5) == k) {
+          cs = a;
+          sn = b;
+        }
+      }
+      c[e] = d < rot ? cs : 1.f;
+      s[e] = d < rot ? (d < half ? -sn : sn) : 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int d = d0 + e;
+      c[e] = 1.f;
+      s[e] = 0.f;
+      if (d < rot) {
+        float sn, cs;
+        sincosf(p * inv.v[d < half ? d : d - half], &sn, &cs);
+        c[e] = cs;
+        s[e] = d < half ? -sn : sn;
+      }
     }
   }
   const int partner = d0 < half ? lane + half / 8 : (d0 < rot ? lane - half / 8 : lane);
