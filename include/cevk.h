@@ -294,7 +294,12 @@ int cevk_gdn_conv(const void* mixed, int32_t mixed_row_stride, const void* conv_
  * the f32 core output before the norm and, for bf16 with dk = dv = 64 or
  * 128, the per-chunk matrices of the tensor-core path.  A workspace of only
  * B*T*nv*dv*4 bytes (the core output) runs every dtype on the f32 SIMT
- * kernel instead. */
+ * kernel instead.  A bf16 dk = dv = 128 call with B = 1, s_out given and at
+ * least 42 chunks (a state run once through the layer), made outside stream
+ * capture, runs in pieces on three streams the library creates per device
+ * on first use, forked from and joined back into `stream` (the next
+ * piece's prep beside the current piece's scan); such calls must not span
+ * a cudaDeviceReset of that device. */
 size_t cevk_gdn_workspace_size(int32_t B, int32_t T, int32_t nv, int32_t dk, int32_t dv);
 int cevk_gdn_chunk_prefill(const void* conv_out, int32_t C, const void* ab, int32_t ab_row_stride, const void* z,
                            int32_t z_row_stride, const float* a_log, const float* dt_bias, const void* norm_w,
