@@ -75,6 +75,14 @@ __device__ __forceinline__ void split8(const float* f, uint4& h, uint4& l) {
   split2(f[6], f[7], h.w, l.w);
 }
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+// Programmatic dependent launch: the scan is launched while the prep still
+// runs (its CTAs take SMs as prep CTAs leave); griddepcontrol.wait holds a
+// thread until the prep grid has completed and its writes are visible, and
+// is a no-op when the kernel was launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
 struct Params {
@@ -176,6 +184,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2) gdn_umma_prep_kernel(Params p
   }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ch = p.c0 + blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  griddep_launch_dependents();  // the scan may be scheduled (it waits for this grid before reading its output)
   const int kh = h / (p.nv / p.nk);  // key head read by this value head (qwen35.rs:436-441)
   const int t0 = ch * C;
   const int key_dim = p.nk * DK;
@@ -659,6 +668,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- operand loads ----------------
+      griddep_wait();  // the records are the prep grid's output
       int n_awq = 0, n_lo = 0, n_rest = 0, n_ai = 0;  // copies issued on each barrier
       for (int c = 0; c < nc; ++c) {
         const uint8_t* rec = p.rec + chunk_index(p, b, p.c0 + c, h) * REC_B;
@@ -794,6 +804,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) gdn_umma_scan_kernel(Params p
     __syncwarp();
     if (lane == 0) mbar_arrive(bar_sready);
     const float* sU = reinterpret_cast<const float*>(smem + S_U);
+    griddep_wait();  // e^last is the prep grid's output
     int c = 0;
     for (; c < nc; ++c) {
       const uint32_t d1 = (c & 1) * 128;
@@ -1034,7 +1045,21 @@ int gdn_umma_run(const void* conv_out, int C_, const void* ab, int ab_rs, const 
     return gdn_umma_pieces(p, GdnNorm{z, z_rs, norm_w, eps, y}, st);
   gum::gdn_umma_prep_kernel<<<dim3(p.n_chunks, nv, B), gum::PREP_THREADS, gum::P_SMEM, st>>>(p);
   if ((rc = check_launch("gdn_umma_prep_kernel"))) return rc;
-  gum::gdn_umma_scan_kernel<<<dim3(gum::DV / gum::NS, nv, B), gum::SCAN_THREADS, gum::S_SMEM, st>>>(p);
+  {  // the scan as a programmatic dependent of the prep
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(gum::DV / gum::NS, nv, B);
+    cfg.blockDim = dim3(gum::SCAN_THREADS);
+    cfg.dynamicSmemBytes = gum::S_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gum::gdn_umma_scan_kernel, p);
+    if (e != cudaSuccess)
+      return set_error(CEVK_E_CUDA, "gdn_umma_scan_kernel: launch: %s", cudaGetErrorString(e));
+  }
   if ((rc = check_launch("gdn_umma_scan_kernel"))) return rc;
   gdn_gated_norm_rows_bf16(p.core, z, z_rs, norm_w, eps, y, 0, (long long)B * T, nv, gum::DV, st);
   return CEVK_OK;
